@@ -1,0 +1,735 @@
+// Flash-attention backward for sm_100a.
+//
+// Replaces the SIMT kernel `flashAttentionBackward<DType>` of the reference
+// (cuda_transformer/flash_attention.cu:226-326).  The reference recomputes
+// P from the saved max and denominator (:298), forms dS = P (dO.V - delta)/sqrt(D)
+// (:299) and scatters dQ/dK/dV with atomics (:317-321); its dK/dV rows are
+// wrong (it mixes the query index into key rows, :312-313).  Here the same
+// recurrence is computed exactly with tensor cores, in three launches:
+//
+//   attn_bwd_prep     delta_i = sum_d O_i[d] dO_i[d]            (HBM-bound)
+//   attn_bwd_dkdv     per key tile (128 keys, stationary K, V); streams
+//                     query tiles (Q, dO) through ST stages:
+//                       S^T  = K Q^T        (SS)   -> TMEM
+//                       dP^T = V dO^T       (SS)   -> TMEM
+//                       P^T  = exp2(S^T*scale*log2e - lse_q*log2e), masked
+//                       dS^T = P^T (dP^T - delta_q) * scale
+//                       dV  += P^T dO       (TS, P^T from TMEM)
+//                       dK  += dS^T Q       (TS, dS^T from TMEM)
+//   attn_bwd_dq       per query tile (stationary Q, dO); streams K/V tiles:
+//                       S  = Q K^T, dP = dO V^T (SS), dS as above (row-wise
+//                       lse/delta), dQ += dS K (TS, dS from TMEM)
+//
+// dQ is produced by its own query-stationary pass instead of atomics, so all
+// three gradients are written once, deterministically, in the I/O type.
+//
+// Warp roles in both main kernels: warps 0..7 = two compute warpgroups that
+// split the 128 score columns (64 each; thread = TMEM lane = row), warp 8 =
+// TMA producer, warp 9 = MMA issuer.  The score buffer S is released as soon
+// as the compute warps have it in registers, so the next S GEMM overlaps the
+// exponentials of the current tile.
+#pragma once
+
+#include "sm100_primitives.cuh"
+
+namespace ctfa {
+
+struct BwdPrepParams {
+  long long rows;    // BH * Tq
+  int Tq;
+  int q_rows_alloc;
+  int q_row0;
+  const void* o;
+  const void* dO;
+  float* delta;      // [BH][Tq]
+};
+
+struct BwdParams {
+  int BH;
+  int Tq, Tk;
+  int q_row0, k_row0;
+  int q_rows_alloc, k_rows_alloc;
+  int causal, causal_offset;
+  float scale;       // 1/sqrt(D)
+  float scale_log2;  // log2(e)/sqrt(D)
+  const float* lse;  // [BH][q_rows_alloc]
+  const float* delta;  // [BH][Tq]
+  void* dq;          // [BH][q_rows_alloc][HD]
+  void* dk;          // [BH][k_rows_alloc][HD]
+  void* dv;
+  unsigned long long wait_limit_ns;
+};
+
+template <typename DT>
+__device__ __forceinline__ float load_as_float(const DT* p) {
+  if constexpr (sizeof(DT) == 4)
+    return *reinterpret_cast<const float*>(p);
+  else if constexpr (std::is_same<DT, __nv_bfloat16>::value)
+    return __bfloat162float(*p);
+  else
+    return __half2float(*p);
+}
+
+// One warp per query row: delta = rowsum(O * dO) in fp32.
+template <typename DT, int HD>
+__global__ void __launch_bounds__(256) attn_bwd_prep(BwdPrepParams p) {
+  const long long w = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= p.rows) return;
+  const long long bh = w / p.Tq, i = w % p.Tq;
+  const size_t row = ((size_t)bh * p.q_rows_alloc + p.q_row0 + i) * HD;
+  const DT* o = reinterpret_cast<const DT*>(p.o) + row;
+  const DT* g = reinterpret_cast<const DT*>(p.dO) + row;
+  float s = 0.f;
+#pragma unroll
+  for (int d = lane; d < HD; d += 32) s += load_as_float(o + d) * load_as_float(g + d);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (lane == 0) p.delta[w] = s;
+}
+
+template <typename DT, int HD>
+struct BwdConfig {
+  static constexpr int BM = 128;  // query rows per tile
+  static constexpr int BN = 128;  // key rows per tile
+  static constexpr int EB = (int)sizeof(DT);
+  static constexpr int E128 = 128 / EB;
+  static constexpr int KBLK = HD * EB / 128;
+  static constexpr int TILE_BYTES = 128 * HD * EB;  // BM == BN == 128
+  static constexpr int KSTEP_S = HD * EB / 32;
+  static constexpr int K_PER = (EB == 4) ? 8 : 16;    // reduction rows per TS MMA
+  static constexpr int KSTEP_T = 128 / K_PER;
+  static constexpr bool TF32 = (EB == 4);
+  static constexpr int ST = (TILE_BYTES * 2 * 3 + TILE_BYTES * 2 <= 200 * 1024) ? 3 : 2;  // streamed stages
+  // dK/dV kernel TMEM map (columns)
+  static constexpr int KV_S = 0;
+  static constexpr int KV_DP = 128;                       // dP^T, then dS^T (tf32) / dS^T packed (16-bit)
+  static constexpr int KV_P = TF32 ? 256 : 160;           // P^T (tf32) / P^T packed: cols [128+64h+32, +32) per half h
+  static constexpr int KV_DK = TF32 ? 384 : 256;
+  static constexpr int KV_DV = KV_DK + HD;
+  static constexpr uint32_t KV_TMEM = tmem_cols_for(KV_DV + HD);
+  // dQ kernel TMEM map
+  static constexpr int Q_S = 0;
+  static constexpr int Q_DP = 128;  // dP, then dS (tf32) / dS packed (16-bit)
+  static constexpr int Q_DQ = 256;
+  static constexpr uint32_t Q_TMEM = tmem_cols_for(Q_DQ + HD);
+  static constexpr int NUM_BARS = 24;
+  static constexpr int SMEM_BYTES = 1024 + 2 * TILE_BYTES + 2 * ST * TILE_BYTES + NUM_BARS * 8 + 16;
+  static constexpr int THREADS = 320;
+  static_assert(KV_DV + HD <= 512, "TMEM budget (dK/dV kernel)");
+  static_assert(HD * EB % 128 == 0, "head dim must fill whole 128-byte rows");
+};
+
+// ---------------------------------------------------------------------------
+// dK / dV
+// ---------------------------------------------------------------------------
+template <typename DT, int HD>
+__global__ void __launch_bounds__(320, 1)
+    attn_bwd_dkdv_sm100(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                        const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                        const BwdParams p) {
+  using C = BwdConfig<DT, HD>;
+  constexpr int ST = C::ST;
+  constexpr int kKind = DTypeTraits<DT>::kKind;
+  constexpr uint32_t kFmt = DTypeTraits<DT>::kFmt;
+  constexpr int TMA_WARP = 8, MMA_WARP = 9;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + C::TILE_BYTES;
+  uint8_t* sQ = sV + C::TILE_BYTES;           // [ST]
+  uint8_t* sdO = sQ + ST * C::TILE_BYTES;     // [ST]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sdO + ST * C::TILE_BYTES);
+  uint64_t* kv_full = bars;
+  uint64_t* q_full = kv_full + 1;   // [ST]
+  uint64_t* q_empty = q_full + ST;  // [ST]
+  uint64_t* s_full = q_empty + ST;
+  uint64_t* s_free = s_full + 1;
+  uint64_t* dp_full = s_free + 1;
+  uint64_t* p_full = dp_full + 1;
+  uint64_t* acc_full = p_full + 1;
+  uint64_t* done_bar = acc_full + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int kt = (int)(blockIdx.x / p.BH);
+  const int bh = (int)(blockIdx.x % p.BH);
+  const int key0 = kt * C::BN;
+
+  // Query tiles that see at least one key of this tile.
+  const int n_qt_all = (p.Tq + C::BM - 1) / C::BM;
+  int qt_first = 0;
+  if (p.causal) {
+    const int need = key0 - p.causal_offset;  // smallest query index that sees key0
+    qt_first = need <= 0 ? 0 : need / C::BM;
+  }
+  const int n_it = max(0, n_qt_all - qt_first);
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&q_full[s], 1);
+      mbar_init(&q_empty[s], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 256);
+    mbar_init(dp_full, 1);
+    mbar_init(p_full, 256);
+    mbar_init(acc_full, 1);
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == MMA_WARP) {
+    tmem_alloc(tmem_holder, C::KV_TMEM);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_holder;
+  const uint64_t limit = p.wait_limit_ns;
+
+  if (warp == TMA_WARP) {
+    if (lane == 0 && n_it > 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      tma_prefetch_desc(&tm_do);
+      mbar_arrive_expect_tx(kv_full, 2 * C::TILE_BYTES);
+#pragma unroll
+      for (int b = 0; b < C::KBLK; ++b) {
+        tma_load_3d(sK + b * 128 * 128, &tm_k, kv_full, b * C::E128, p.k_row0 + key0, bh);
+        tma_load_3d(sV + b * 128 * 128, &tm_v, kv_full, b * C::E128, p.k_row0 + key0, bh);
+      }
+      int issued = 0;
+      for (int it = 0; it < n_it; ++it) {
+        const int st = it % ST;
+        if (!mbar_wait(&q_empty[st], ((it / ST) & 1) ^ 1, abort_flag, limit, 11)) break;
+        const int row = p.q_row0 + (qt_first + it) * C::BM;
+        mbar_arrive_expect_tx(&q_full[st], 2 * C::TILE_BYTES);
+#pragma unroll
+        for (int b = 0; b < C::KBLK; ++b) {
+          tma_load_3d(sQ + st * C::TILE_BYTES + b * 128 * 128, &tm_q, &q_full[st], b * C::E128, row, bh);
+          tma_load_3d(sdO + st * C::TILE_BYTES + b * 128 * 128, &tm_do, &q_full[st], b * C::E128, row, bh);
+        }
+        issued = it + 1;
+      }
+      if (*abort_flag) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(kv_full, 0) && globaltimer_ns() - t0 < limit) {
+        }
+        for (int it = max(0, issued - ST); it < issued; ++it)
+          while (!mbar_try_wait(&q_full[it % ST], (it / ST) & 1) && globaltimer_ns() - t0 < limit) {
+          }
+      }
+    }
+    __syncwarp();
+  } else if (warp == MMA_WARP) {
+    if (lane == 0 && n_it > 0) {
+      constexpr uint32_t idesc_s = make_idesc(kFmt, 128, 128, false, false);
+      constexpr uint32_t idesc_t = make_idesc(kFmt, 128, HD, false, true);
+      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ), adO = smem_u32(sdO);
+      auto gemm_ss = [&](uint32_t d, uint32_t a_base, uint32_t b_base) {
+#pragma unroll
+        for (int ks = 0; ks < C::KSTEP_S; ++ks) {
+          const uint32_t off = (ks >> 2) * (128 * 128) + (ks & 3) * 32;
+          umma_ss<kKind>(d, make_sdesc_sw128(a_base + off, 16, 1024), make_sdesc_sw128(b_base + off, 16, 1024),
+                         idesc_s, ks > 0 ? 1u : 0u);
+        }
+      };
+      // A operand columns: tf32 operands are contiguous; 16-bit operands are
+      // packed by each compute warpgroup into its own 64-column half.
+      auto gemm_ts = [&](uint32_t d, uint32_t a_tmem, uint32_t b_base, bool acc) {
+#pragma unroll
+        for (int ks = 0; ks < C::KSTEP_T; ++ks) {
+          const uint32_t a_col = C::TF32 ? ks * 8 : (ks >> 2) * 64 + (ks & 3) * 8;
+          umma_ts<kKind>(d, a_tmem + a_col, make_sdesc_sw128(b_base + ks * C::K_PER * 128, 128 * 128, 1024),
+                         idesc_t, (acc || ks > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(kv_full, 0, abort_flag, limit, 12) && mbar_wait(&q_full[0], 0, abort_flag, limit, 13);
+      if (ok) {
+        tc_fence_after();
+        gemm_ss(tbase + C::KV_S, aK, aQ);
+        umma_commit(s_full);
+        gemm_ss(tbase + C::KV_DP, aV, adO);
+        umma_commit(dp_full);
+      }
+      for (int it = 0; ok && it < n_it; ++it) {
+        const int st = it % ST;
+        const int st1 = (it + 1) % ST;
+        if (it + 1 < n_it) {
+          if (!(ok = mbar_wait(s_free, it & 1, abort_flag, limit, 14))) break;
+          if (!(ok = mbar_wait(&q_full[st1], ((it + 1) / ST) & 1, abort_flag, limit, 15))) break;
+          tc_fence_after();
+          gemm_ss(tbase + C::KV_S, aK, aQ + st1 * C::TILE_BYTES);
+          umma_commit(s_full);
+        }
+        if (!(ok = mbar_wait(p_full, it & 1, abort_flag, limit, 16))) break;
+        tc_fence_after();
+        gemm_ts(tbase + C::KV_DV, tbase + C::KV_P, adO + st * C::TILE_BYTES, it > 0);
+        gemm_ts(tbase + C::KV_DK, tbase + C::KV_DP, aQ + st * C::TILE_BYTES, it > 0);
+        umma_commit(&q_empty[st]);
+        if (it + 1 < n_it) {
+          gemm_ss(tbase + C::KV_DP, aV, adO + st1 * C::TILE_BYTES);
+          umma_commit(dp_full);
+        } else {
+          umma_commit(acc_full);
+        }
+      }
+      umma_commit(done_bar);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(done_bar, 0) && globaltimer_ns() - t0 < limit) {
+      }
+    }
+    __syncwarp();
+  } else {
+    // --------------------------- compute warps ---------------------------
+    const int h = threadIdx.x >> 7;  // column half
+    const int r = threadIdx.x & 127; // key row inside the tile (TMEM lane)
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const int key = key0 + r;
+    const float sl2 = p.scale_log2;
+    const float scale = p.scale;
+    const float* lse_bh = p.lse + (size_t)bh * p.q_rows_alloc + p.q_row0;
+    const float* delta_bh = p.delta + (size_t)bh * p.Tq;
+    bool ok = true;
+    for (int it = 0; it < n_it; ++it) {
+      const int q0 = (qt_first + it) * C::BM + h * 64;
+      if (!(ok = mbar_wait(s_full, it & 1, abort_flag, limit, 17))) break;
+      tc_fence_after();
+      float s[64];
+      {
+        uint32_t regs[32];
+        tmem_ld32(tbase + lane_off + C::KV_S + h * 64, regs);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[i] = __uint_as_float(regs[i]);
+        tmem_ld32(tbase + lane_off + C::KV_S + h * 64 + 32, regs);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[32 + i] = __uint_as_float(regs[i]);
+      }
+      tc_fence_before();
+      mbar_arrive(s_free);
+      // P^T = exp2(S^T * scale*log2e - lse*log2e), masked.
+      const bool key_ok = key < p.Tk;
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const int q = q0 + c;
+        const bool vis = key_ok && q < p.Tq && (!p.causal || key <= q + p.causal_offset);
+        const float L = vis ? __ldg(lse_bh + q) * 1.4426950408889634f : 0.f;
+        s[c] = vis ? ex2_approx(fmaf(s[c], sl2, -L)) : 0.f;
+      }
+      if (!(ok = mbar_wait(dp_full, it & 1, abort_flag, limit, 18))) break;
+      tc_fence_after();
+      float dsv[64];
+      {
+        uint32_t regs[32];
+        tmem_ld32(tbase + lane_off + C::KV_DP + h * 64, regs);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) dsv[i] = __uint_as_float(regs[i]);
+        tmem_ld32(tbase + lane_off + C::KV_DP + h * 64 + 32, regs);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) dsv[32 + i] = __uint_as_float(regs[i]);
+      }
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const int q = q0 + c;
+        const float dl = q < p.Tq ? __ldg(delta_bh + q) : 0.f;
+        dsv[c] = s[c] * (dsv[c] - dl) * scale;
+      }
+      if constexpr (C::TF32) {
+        uint32_t regs[32];
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) regs[i] = f32_to_tf32_rna(s[half * 32 + i]);
+          tmem_st32(tbase + lane_off + C::KV_P + h * 64 + half * 32, regs);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) regs[i] = f32_to_tf32_rna(dsv[half * 32 + i]);
+          tmem_st32(tbase + lane_off + C::KV_DP + h * 64 + half * 32, regs);
+        }
+      } else {
+        uint32_t regs[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          regs[i] = (kFmt == 1) ? pack_bf16x2(s[2 * i], s[2 * i + 1]) : pack_f16x2(s[2 * i], s[2 * i + 1]);
+        tmem_st32(tbase + lane_off + C::KV_DP + h * 64 + 32, regs);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          regs[i] = (kFmt == 1) ? pack_bf16x2(dsv[2 * i], dsv[2 * i + 1]) : pack_f16x2(dsv[2 * i], dsv[2 * i + 1]);
+        tmem_st32(tbase + lane_off + C::KV_DP + h * 64, regs);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    // ------------------------------ epilogue ------------------------------
+    if (ok && n_it > 0) ok = mbar_wait(acc_full, 0, abort_flag, limit, 19);
+    if (ok) {
+      tc_fence_after();
+      const bool row_ok = key < p.Tk;
+      const size_t row_index = (size_t)bh * p.k_rows_alloc + p.k_row0 + key;
+      DT* dk_row = reinterpret_cast<DT*>(p.dk) + row_index * HD;
+      DT* dv_row = reinterpret_cast<DT*>(p.dv) + row_index * HD;
+#pragma unroll
+      for (int c = 0; c < HD / 64; ++c) {
+        const int col = h * (HD / 2) + c * 32;
+#pragma unroll
+        for (int which = 0; which < 2; ++which) {
+          uint32_t regs[32];
+          if (n_it > 0) {
+            tmem_ld32(tbase + lane_off + (which ? C::KV_DV : C::KV_DK) + col, regs);
+            tmem_wait_ld();
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) regs[i] = 0u;
+          }
+          if (row_ok) {
+            DT* dst = (which ? dv_row : dk_row) + col;
+            if constexpr (C::EB == 4) {
+              float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                d4[i] = make_float4(__uint_as_float(regs[4 * i]), __uint_as_float(regs[4 * i + 1]),
+                                    __uint_as_float(regs[4 * i + 2]), __uint_as_float(regs[4 * i + 3]));
+            } else {
+              uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                uint32_t w[4];
+#pragma unroll
+                for (int hh = 0; hh < 4; ++hh) {
+                  const float a = __uint_as_float(regs[8 * i + 2 * hh]);
+                  const float b = __uint_as_float(regs[8 * i + 2 * hh + 1]);
+                  w[hh] = (kFmt == 1) ? pack_bf16x2(a, b) : pack_f16x2(a, b);
+                }
+                d4[i] = make_uint4(w[0], w[1], w[2], w[3]);
+              }
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == MMA_WARP) {
+    tc_fence_after();
+    tmem_dealloc(tbase, C::KV_TMEM);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// dQ
+// ---------------------------------------------------------------------------
+template <typename DT, int HD>
+__global__ void __launch_bounds__(320, 1)
+    attn_bwd_dq_sm100(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                      const BwdParams p, int n_qtiles) {
+  using C = BwdConfig<DT, HD>;
+  constexpr int ST = C::ST;
+  constexpr int kKind = DTypeTraits<DT>::kKind;
+  constexpr uint32_t kFmt = DTypeTraits<DT>::kFmt;
+  constexpr int TMA_WARP = 8, MMA_WARP = 9;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sdO = sQ + C::TILE_BYTES;
+  uint8_t* sK = sdO + C::TILE_BYTES;   // [ST]
+  uint8_t* sV = sK + ST * C::TILE_BYTES;  // [ST]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + ST * C::TILE_BYTES);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = q_full + 1;    // [ST]
+  uint64_t* k_empty = k_full + ST;  // [ST]
+  uint64_t* v_full = k_empty + ST;  // [ST]
+  uint64_t* v_empty = v_full + ST;  // [ST]
+  uint64_t* s_full = v_empty + ST;
+  uint64_t* s_free = s_full + 1;
+  uint64_t* dp_full = s_free + 1;
+  uint64_t* ds_full = dp_full + 1;
+  uint64_t* acc_full = ds_full + 1;
+  uint64_t* done_bar = acc_full + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  int qt, bh;
+  if (p.causal) {  // heavy query tiles first
+    qt = n_qtiles - 1 - (int)(blockIdx.x / p.BH);
+    bh = (int)(blockIdx.x % p.BH);
+  } else {
+    qt = (int)(blockIdx.x % n_qtiles);
+    bh = (int)(blockIdx.x / n_qtiles);
+  }
+  const int n_kv_all = (p.Tk + C::BN - 1) / C::BN;
+  int n_kv = n_kv_all;
+  if (p.causal) {
+    const int last_row = min(qt * C::BM + C::BM - 1, p.Tq - 1) + p.causal_offset;
+    n_kv = last_row < 0 ? 0 : min(n_kv_all, last_row / C::BN + 1);
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 256);
+    mbar_init(dp_full, 1);
+    mbar_init(ds_full, 256);
+    mbar_init(acc_full, 1);
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == MMA_WARP) {
+    tmem_alloc(tmem_holder, C::Q_TMEM);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_holder;
+  const uint64_t limit = p.wait_limit_ns;
+
+  if (warp == TMA_WARP) {
+    if (lane == 0 && n_kv > 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      tma_prefetch_desc(&tm_do);
+      const int qrow = p.q_row0 + qt * C::BM;
+      mbar_arrive_expect_tx(q_full, 2 * C::TILE_BYTES);
+#pragma unroll
+      for (int b = 0; b < C::KBLK; ++b) {
+        tma_load_3d(sQ + b * 128 * 128, &tm_q, q_full, b * C::E128, qrow, bh);
+        tma_load_3d(sdO + b * 128 * 128, &tm_do, q_full, b * C::E128, qrow, bh);
+      }
+      int issued_k = 0, issued_v = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j % ST;
+        const uint32_t ph = (j / ST) & 1;
+        const int row = p.k_row0 + j * C::BN;
+        if (!mbar_wait(&k_empty[st], ph ^ 1, abort_flag, limit, 21)) break;
+        mbar_arrive_expect_tx(&k_full[st], C::TILE_BYTES);
+#pragma unroll
+        for (int b = 0; b < C::KBLK; ++b)
+          tma_load_3d(sK + st * C::TILE_BYTES + b * 128 * 128, &tm_k, &k_full[st], b * C::E128, row, bh);
+        issued_k = j + 1;
+        if (!mbar_wait(&v_empty[st], ph ^ 1, abort_flag, limit, 22)) break;
+        mbar_arrive_expect_tx(&v_full[st], C::TILE_BYTES);
+#pragma unroll
+        for (int b = 0; b < C::KBLK; ++b)
+          tma_load_3d(sV + st * C::TILE_BYTES + b * 128 * 128, &tm_v, &v_full[st], b * C::E128, row, bh);
+        issued_v = j + 1;
+      }
+      if (*abort_flag) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(q_full, 0) && globaltimer_ns() - t0 < limit) {
+        }
+        for (int j = max(0, issued_k - ST); j < issued_k; ++j)
+          while (!mbar_try_wait(&k_full[j % ST], (j / ST) & 1) && globaltimer_ns() - t0 < limit) {
+          }
+        for (int j = max(0, issued_v - ST); j < issued_v; ++j)
+          while (!mbar_try_wait(&v_full[j % ST], (j / ST) & 1) && globaltimer_ns() - t0 < limit) {
+          }
+      }
+    }
+    __syncwarp();
+  } else if (warp == MMA_WARP) {
+    if (lane == 0 && n_kv > 0) {
+      constexpr uint32_t idesc_s = make_idesc(kFmt, 128, 128, false, false);
+      constexpr uint32_t idesc_t = make_idesc(kFmt, 128, HD, false, true);
+      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ), adO = smem_u32(sdO);
+      auto gemm_ss = [&](uint32_t d, uint32_t a_base, uint32_t b_base) {
+#pragma unroll
+        for (int ks = 0; ks < C::KSTEP_S; ++ks) {
+          const uint32_t off = (ks >> 2) * (128 * 128) + (ks & 3) * 32;
+          umma_ss<kKind>(d, make_sdesc_sw128(a_base + off, 16, 1024), make_sdesc_sw128(b_base + off, 16, 1024),
+                         idesc_s, ks > 0 ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(q_full, 0, abort_flag, limit, 23) && mbar_wait(&k_full[0], 0, abort_flag, limit, 24) &&
+                mbar_wait(&v_full[0], 0, abort_flag, limit, 25);
+      if (ok) {
+        tc_fence_after();
+        gemm_ss(tbase + C::Q_S, aQ, aK);
+        umma_commit(s_full);
+        gemm_ss(tbase + C::Q_DP, adO, aV);
+        umma_commit(dp_full);
+        umma_commit(&v_empty[0]);
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int st = j % ST;
+        const int st1 = (j + 1) % ST;
+        const uint32_t ph1 = ((j + 1) / ST) & 1;
+        if (j + 1 < n_kv) {
+          if (!(ok = mbar_wait(s_free, j & 1, abort_flag, limit, 26))) break;
+          if (!(ok = mbar_wait(&k_full[st1], ph1, abort_flag, limit, 27))) break;
+          tc_fence_after();
+          gemm_ss(tbase + C::Q_S, aQ, aK + st1 * C::TILE_BYTES);
+          umma_commit(s_full);
+        }
+        if (!(ok = mbar_wait(ds_full, j & 1, abort_flag, limit, 28))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < C::KSTEP_T; ++ks) {
+          const uint32_t a_col = C::TF32 ? ks * 8 : (ks >> 2) * 64 + (ks & 3) * 8;
+          umma_ts<kKind>(tbase + C::Q_DQ, tbase + C::Q_DP + a_col,
+                         make_sdesc_sw128(aK + st * C::TILE_BYTES + ks * C::K_PER * 128, 128 * 128, 1024), idesc_t,
+                         (j > 0 || ks > 0) ? 1u : 0u);
+        }
+        umma_commit(&k_empty[st]);
+        if (j + 1 < n_kv) {
+          if (!(ok = mbar_wait(&v_full[st1], ph1, abort_flag, limit, 29))) break;
+          tc_fence_after();
+          gemm_ss(tbase + C::Q_DP, adO, aV + st1 * C::TILE_BYTES);
+          umma_commit(dp_full);
+          umma_commit(&v_empty[st1]);
+        } else {
+          umma_commit(acc_full);
+        }
+      }
+      umma_commit(done_bar);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(done_bar, 0) && globaltimer_ns() - t0 < limit) {
+      }
+    }
+    __syncwarp();
+  } else {
+    // --------------------------- compute warps ---------------------------
+    const int h = threadIdx.x >> 7;   // key-column half
+    const int r = threadIdx.x & 127;  // query row (TMEM lane)
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const int q = qt * C::BM + r;
+    const bool q_ok = q < p.Tq;
+    const float sl2 = p.scale_log2;
+    const float scale = p.scale;
+    const size_t lrow = (size_t)bh * p.q_rows_alloc + p.q_row0 + q;
+    const float L = q_ok ? p.lse[lrow] * 1.4426950408889634f : 0.f;
+    const float dl = q_ok ? p.delta[(size_t)bh * p.Tq + q] : 0.f;
+    int vis = p.Tk - 1;
+    if (p.causal) vis = min(vis, q + p.causal_offset);
+    if (!q_ok) vis = -1;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      const int kc0 = j * C::BN + h * 64;  // first key of this thread's half
+      if (!(ok = mbar_wait(s_full, j & 1, abort_flag, limit, 30))) break;
+      tc_fence_after();
+      float s[64];
+      {
+        uint32_t regs[32];
+        tmem_ld32(tbase + lane_off + C::Q_S + h * 64, regs);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[i] = __uint_as_float(regs[i]);
+        tmem_ld32(tbase + lane_off + C::Q_S + h * 64 + 32, regs);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[32 + i] = __uint_as_float(regs[i]);
+      }
+      tc_fence_before();
+      mbar_arrive(s_free);
+      const int lim = vis - kc0;
+#pragma unroll
+      for (int c = 0; c < 64; ++c) s[c] = (c <= lim) ? ex2_approx(fmaf(s[c], sl2, -L)) : 0.f;
+      if (!(ok = mbar_wait(dp_full, j & 1, abort_flag, limit, 31))) break;
+      tc_fence_after();
+      float dsv[64];
+      {
+        uint32_t regs[32];
+        tmem_ld32(tbase + lane_off + C::Q_DP + h * 64, regs);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) dsv[i] = __uint_as_float(regs[i]);
+        tmem_ld32(tbase + lane_off + C::Q_DP + h * 64 + 32, regs);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) dsv[32 + i] = __uint_as_float(regs[i]);
+      }
+#pragma unroll
+      for (int c = 0; c < 64; ++c) dsv[c] = s[c] * (dsv[c] - dl) * scale;
+      if constexpr (C::TF32) {
+        uint32_t regs[32];
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) regs[i] = f32_to_tf32_rna(dsv[half * 32 + i]);
+          tmem_st32(tbase + lane_off + C::Q_DP + h * 64 + half * 32, regs);
+        }
+      } else {
+        uint32_t regs[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          regs[i] = (kFmt == 1) ? pack_bf16x2(dsv[2 * i], dsv[2 * i + 1]) : pack_f16x2(dsv[2 * i], dsv[2 * i + 1]);
+        tmem_st32(tbase + lane_off + C::Q_DP + h * 64, regs);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(ds_full);
+    }
+    if (ok && n_kv > 0) ok = mbar_wait(acc_full, 0, abort_flag, limit, 32);
+    if (ok) {
+      tc_fence_after();
+      DT* dq_row = reinterpret_cast<DT*>(p.dq) + lrow * HD;
+#pragma unroll
+      for (int c = 0; c < HD / 64; ++c) {
+        const int col = h * (HD / 2) + c * 32;
+        uint32_t regs[32];
+        if (n_kv > 0) {
+          tmem_ld32(tbase + lane_off + C::Q_DQ + col, regs);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) regs[i] = 0u;
+        }
+        if (q_ok) {
+          if constexpr (C::EB == 4) {
+            float4* d4 = reinterpret_cast<float4*>(dq_row + col);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              d4[i] = make_float4(__uint_as_float(regs[4 * i]), __uint_as_float(regs[4 * i + 1]),
+                                  __uint_as_float(regs[4 * i + 2]), __uint_as_float(regs[4 * i + 3]));
+          } else {
+            uint4* d4 = reinterpret_cast<uint4*>(dq_row + col);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              uint32_t w[4];
+#pragma unroll
+              for (int hh = 0; hh < 4; ++hh) {
+                const float a = __uint_as_float(regs[8 * i + 2 * hh]);
+                const float b = __uint_as_float(regs[8 * i + 2 * hh + 1]);
+                w[hh] = (kFmt == 1) ? pack_bf16x2(a, b) : pack_f16x2(a, b);
+              }
+              d4[i] = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == MMA_WARP) {
+    tc_fence_after();
+    tmem_dealloc(tbase, C::Q_TMEM);
+  }
+}
+
+}  // namespace ctfa

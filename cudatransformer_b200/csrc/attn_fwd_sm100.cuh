@@ -1,0 +1,431 @@
+// Flash-attention forward for sm_100a: TMA -> 128B-swizzled shared memory,
+// tcgen05.mma with S and O accumulators in TMEM, online softmax in registers.
+//
+// Replaces the SIMT kernel `flashAttention<DType>` of the reference
+// (cuda_transformer/flash_attention.cu:57-169), which streams 32-key tiles
+// through shared memory with scalar dot products.  The math is the same
+// online-softmax recurrence (running max, rescaled denominator, rescaled
+// weighted sum: flash_attention.cu:120-153); what changes is where it runs:
+//
+//   CTA  = NQ query tiles of 128 rows of one (batch, head), sharing K/V tiles.
+//   warps 0..4*NQ-1 : softmax, one warpgroup per query tile, one thread per
+//                     query row (= TMEM lane).
+//   warp  4*NQ      : TMA producer (Q once, then K/V tiles through ST stages).
+//   warp  4*NQ+1    : tcgen05.mma issuer (one elected lane).
+//
+//   TMEM columns:  S_k = Q_k K^T  at [k*BN, (k+1)*BN)            (fp32)
+//                  P_k written over S_k by the softmax warps       (tf32, or bf16/fp16 packed in pairs)
+//                  O_k += P_k V   at [NQ*BN + k*HD, ... + HD)      (fp32)
+//
+// The MMA warp alternates the query tiles (ping-pong): while the softmax of
+// tile 0 runs, the tensor core computes P_1 V and the next S_1, and vice versa.
+// The running max is rescaled lazily: O is only rescaled when the max grows by
+// more than 2^8 (log2 domain), which keeps the exponentials below 256.
+//
+// Masking: key j (local to the call) is visible to query i iff j < Tk and,
+// when causal, j <= i + causal_offset.  The reference has no causal mode and
+// treats keys past T as zero vectors that still enter the softmax
+// (flash_attention.cu:104-109); here they are excluded.
+#pragma once
+
+#include "sm100_primitives.cuh"
+
+namespace ctfa {
+
+struct FwdParams {
+  int BH;              // batch * heads
+  int Tq, Tk;          // query rows / key rows handled by this call (per head)
+  int q_row0, k_row0;  // first row of this call inside each head's allocation
+  int q_rows_alloc;    // rows per head in the Q/O/LSE allocations
+  int causal;          // 0: every key visible; 1: key j visible iff j <= i + causal_offset
+  int causal_offset;
+  int n_groups;        // CTA groups of NQ query tiles per head
+  float scale_log2;    // softmax scale * log2(e)
+  void* o;             // [BH][q_rows_alloc][HD] DT
+  float* lse;          // [BH][q_rows_alloc] natural-log logsumexp (nullable)
+  unsigned long long wait_limit_ns;
+};
+
+template <typename DT, int HD, int NQ, int BN, int ST>
+struct FwdConfig {
+  static constexpr int BM = 128;
+  static constexpr int EB = (int)sizeof(DT);
+  static constexpr int E128 = 128 / EB;           // elements per 128-byte row segment
+  static constexpr int KBLK = HD * EB / 128;      // 128-byte column blocks per row
+  static constexpr int Q_TILE_BYTES = BM * HD * EB;
+  static constexpr int KV_TILE_BYTES = BN * HD * EB;
+  static constexpr int KSTEP_S = HD * EB / 32;    // QK^T k-steps (32 bytes of head dim each)
+  static constexpr int K_PER_PV = (EB == 4) ? 8 : 16;
+  static constexpr int KSTEP_PV = BN / K_PER_PV;
+  static constexpr int P_COLS = (EB == 4) ? BN : BN / 2;
+  static constexpr uint32_t TMEM_COLS = tmem_cols_for(NQ * (BN + HD));
+  static constexpr int NUM_BARS = 1 + 4 * ST + 3 * NQ + 1;
+  static constexpr int SMEM_BYTES = 1024 + NQ * Q_TILE_BYTES + 2 * ST * KV_TILE_BYTES + NUM_BARS * 8 + 16;
+  static constexpr int THREADS = NQ * 128 + 64;
+  static_assert(HD * EB % 128 == 0, "head dim must fill whole 128-byte rows");
+  static_assert(BN % 32 == 0 && BN <= 256, "key tile");
+  static_assert(NQ * (BN + HD) <= 512, "TMEM budget");
+};
+
+template <typename DT, int HD, int NQ, int BN, int ST>
+__global__ void __launch_bounds__(NQ * 128 + 64, 1)
+    attn_fwd_sm100(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                   const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
+  using C = FwdConfig<DT, HD, NQ, BN, ST>;
+  constexpr int BM = C::BM;
+  constexpr int kKind = DTypeTraits<DT>::kKind;
+  constexpr uint32_t kFmt = DTypeTraits<DT>::kFmt;
+  constexpr int TMA_WARP = NQ * 4;
+  constexpr int MMA_WARP = NQ * 4 + 1;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + NQ * C::Q_TILE_BYTES;
+  uint8_t* sV = sK + ST * C::KV_TILE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + ST * C::KV_TILE_BYTES);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = q_full + 1;
+  uint64_t* k_empty = k_full + ST;
+  uint64_t* v_full = k_empty + ST;
+  uint64_t* v_empty = v_full + ST;
+  uint64_t* s_full = v_empty + ST;
+  uint64_t* p_full = s_full + NQ;
+  uint64_t* o_full = p_full + NQ;
+  uint64_t* done_bar = o_full + NQ;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // ---- work assignment: heavy query groups first under the causal mask ----
+  int group, bh;
+  if (p.causal) {
+    group = p.n_groups - 1 - (int)(blockIdx.x / p.BH);
+    bh = (int)(blockIdx.x % p.BH);
+  } else {
+    group = (int)(blockIdx.x % p.n_groups);
+    bh = (int)(blockIdx.x / p.n_groups);
+  }
+  const int n_kv_all = (p.Tk + BN - 1) / BN;
+  int n_kv[NQ];
+  int n_max = 0;
+#pragma unroll
+  for (int k = 0; k < NQ; ++k) {
+    const int qt = group * NQ + k;
+    int n = 0;
+    if (qt * BM < p.Tq) {
+      n = n_kv_all;
+      if (p.causal) {
+        const int last_row = min(qt * BM + BM - 1, p.Tq - 1) + p.causal_offset;
+        n = last_row < 0 ? 0 : min(n_kv_all, last_row / BN + 1);
+      }
+    }
+    n_kv[k] = n;
+    n_max = max(n_max, n);
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int k = 0; k < NQ; ++k) {
+      mbar_init(&s_full[k], 1);
+      mbar_init(&p_full[k], 128);
+      mbar_init(&o_full[k], 1);
+    }
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == MMA_WARP) {
+    tmem_alloc(tmem_holder, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_holder;
+  const uint64_t limit = p.wait_limit_ns;
+
+  if (warp == TMA_WARP) {
+    if (lane == 0 && n_max > 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      int q_bytes = 0;
+#pragma unroll
+      for (int k = 0; k < NQ; ++k) q_bytes += (n_kv[k] > 0) ? C::Q_TILE_BYTES : 0;
+      mbar_arrive_expect_tx(q_full, q_bytes);
+#pragma unroll
+      for (int k = 0; k < NQ; ++k) {
+        if (n_kv[k] == 0) continue;
+        const int row = p.q_row0 + (group * NQ + k) * BM;
+#pragma unroll
+        for (int b = 0; b < C::KBLK; ++b)
+          tma_load_3d(sQ + k * C::Q_TILE_BYTES + b * BM * 128, &tm_q, q_full, b * C::E128, row, bh);
+      }
+      int issued_k = 0, issued_v = 0;
+      for (int j = 0; j < n_max; ++j) {
+        const int st = j % ST;
+        const uint32_t ph = (j / ST) & 1;
+        const int row = p.k_row0 + j * BN;
+        if (!mbar_wait(&k_empty[st], ph ^ 1, abort_flag, limit, 1)) break;
+        mbar_arrive_expect_tx(&k_full[st], C::KV_TILE_BYTES);
+#pragma unroll
+        for (int b = 0; b < C::KBLK; ++b)
+          tma_load_3d(sK + st * C::KV_TILE_BYTES + b * BN * 128, &tm_k, &k_full[st], b * C::E128, row, bh);
+        issued_k = j + 1;
+        if (!mbar_wait(&v_empty[st], ph ^ 1, abort_flag, limit, 2)) break;
+        mbar_arrive_expect_tx(&v_full[st], C::KV_TILE_BYTES);
+#pragma unroll
+        for (int b = 0; b < C::KBLK; ++b)
+          tma_load_3d(sV + st * C::KV_TILE_BYTES + b * BN * 128, &tm_v, &v_full[st], b * C::E128, row, bh);
+        issued_v = j + 1;
+      }
+      // On an aborted run some loads may still be landing: wait (bounded,
+      // ignoring the abort flag) for the last load issued into each stage.
+      if (*abort_flag) {
+        const uint64_t t0 = globaltimer_ns();
+        for (int j = max(0, issued_k - ST); j < issued_k; ++j)
+          while (!mbar_try_wait(&k_full[j % ST], (j / ST) & 1) && globaltimer_ns() - t0 < limit) {
+          }
+        for (int j = max(0, issued_v - ST); j < issued_v; ++j)
+          while (!mbar_try_wait(&v_full[j % ST], (j / ST) & 1) && globaltimer_ns() - t0 < limit) {
+          }
+        while (!mbar_try_wait(q_full, 0) && globaltimer_ns() - t0 < limit) {
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == MMA_WARP) {
+    if (lane == 0 && n_max > 0) {
+      constexpr uint32_t idesc_s = make_idesc(kFmt, 128, BN, false, false);
+      constexpr uint32_t idesc_pv = make_idesc(kFmt, 128, HD, false, true);
+      const uint32_t sQ_addr = smem_u32(sQ);
+      const uint32_t sK_addr = smem_u32(sK);
+      const uint32_t sV_addr = smem_u32(sV);
+
+      auto issue_s = [&](int k, int st) {
+        const uint32_t d = tbase + k * BN;
+#pragma unroll
+        for (int ks = 0; ks < C::KSTEP_S; ++ks) {
+          const uint64_t a = make_sdesc_sw128(sQ_addr + k * C::Q_TILE_BYTES + (ks >> 2) * (BM * 128) + (ks & 3) * 32,
+                                              16, 1024);
+          const uint64_t b = make_sdesc_sw128(
+              sK_addr + st * C::KV_TILE_BYTES + (ks >> 2) * (BN * 128) + (ks & 3) * 32, 16, 1024);
+          umma_ss<kKind>(d, a, b, idesc_s, ks > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_pv = [&](int k, int st, bool acc) {
+        const uint32_t d = tbase + NQ * BN + k * HD;
+#pragma unroll
+        for (int ks = 0; ks < C::KSTEP_PV; ++ks) {
+          const uint32_t a = tbase + k * BN + ks * 8;
+          const uint64_t b =
+              make_sdesc_sw128(sV_addr + st * C::KV_TILE_BYTES + ks * C::K_PER_PV * 128, BN * 128, 1024);
+          umma_ts<kKind>(d, a, b, idesc_pv, (acc || ks > 0) ? 1u : 0u);
+        }
+      };
+
+      bool ok = mbar_wait(q_full, 0, abort_flag, limit, 3);
+      if (ok) ok = mbar_wait(&k_full[0], 0, abort_flag, limit, 4);
+      if (ok) {
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < NQ; ++k) {
+          if (n_kv[k] > 0) {
+            issue_s(k, 0);
+            umma_commit(&s_full[k]);
+          }
+        }
+        umma_commit(&k_empty[0]);
+      }
+      for (int j = 0; ok && j < n_max; ++j) {
+        const int st = j % ST;
+        const int st1 = (j + 1) % ST;
+        if (!(ok = mbar_wait(&v_full[st], (j / ST) & 1, abort_flag, limit, 5))) break;
+        bool next_k = false;
+#pragma unroll
+        for (int k = 0; k < NQ; ++k) {
+          if (j >= n_kv[k]) continue;
+          if (!(ok = mbar_wait(&p_full[k], j & 1, abort_flag, limit, 6))) break;
+          tc_fence_after();
+          issue_pv(k, st, j > 0);
+          if (j == n_kv[k] - 1) umma_commit(&o_full[k]);
+          if (j + 1 < n_kv[k]) {
+            if (!next_k) {
+              if (!(ok = mbar_wait(&k_full[st1], ((j + 1) / ST) & 1, abort_flag, limit, 7))) break;
+              tc_fence_after();
+              next_k = true;
+            }
+            issue_s(k, st1);
+            umma_commit(&s_full[k]);
+          }
+        }
+        umma_commit(&v_empty[st]);
+        if (next_k) umma_commit(&k_empty[st1]);
+      }
+      // Wait (bounded, regardless of abort) for every MMA issued so far, so
+      // that TMEM is idle before it is released.
+      umma_commit(done_bar);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(done_bar, 0) && globaltimer_ns() - t0 < limit) {
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------- softmax warps ----------------------------
+    const int k = threadIdx.x >> 7;          // query tile inside the CTA
+    const int r = threadIdx.x & 127;         // row inside the tile (TMEM lane)
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const int qt = group * NQ + k;
+    const int q_local = qt * BM + r;
+    const int n = n_kv[k];
+    const uint32_t s_addr = tbase + lane_off + k * BN;
+    const uint32_t o_addr = tbase + lane_off + NQ * BN + k * HD;
+    const float sl2 = p.scale_log2;
+    float m = -INFINITY;
+    float l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      if (!(ok = mbar_wait(&s_full[k], j & 1, abort_flag, limit, 8))) break;
+      tc_fence_after();
+      float s[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t regs[32];
+        tmem_ld32(s_addr + c * 32, regs);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(regs[i]);
+      }
+      const int key0 = j * BN;
+      int vis = p.Tk - 1;  // last visible key for this row
+      int vis_tile = p.Tk - 1;
+      if (p.causal) {
+        vis = min(vis, q_local + p.causal_offset);
+        vis_tile = min(vis_tile, qt * BM + p.causal_offset);
+      }
+      if (key0 + BN - 1 > vis_tile) {
+        const int lim = vis - key0;
+#pragma unroll
+        for (int c = 0; c < BN; ++c)
+          if (c > lim) s[c] = -INFINITY;
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BN; ++c) mx = fmaxf(mx, s[c]);
+      mx *= sl2;
+      if (j == 0) {
+        m = mx;
+      } else {
+        const bool need = mx > m + 8.f;
+        if (__any_sync(0xffffffffu, need)) {
+          const float m_new = fmaxf(m, mx);
+          const float alpha = (m == -INFINITY) ? 0.f : ex2_approx(m - m_new);
+          l *= alpha;
+          m = m_new;
+#pragma unroll
+          for (int c = 0; c < HD / 32; ++c) {
+            uint32_t regs[32];
+            tmem_ld32(o_addr + c * 32, regs);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) regs[i] = __float_as_uint(__uint_as_float(regs[i]) * alpha);
+            tmem_st32(o_addr + c * 32, regs);
+          }
+        }
+      }
+      const float m_use = (m == -INFINITY) ? 0.f : m;
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < BN; ++c) {
+        s[c] = ex2_approx(fmaf(s[c], sl2, -m_use));
+        rs += s[c];
+      }
+      l += rs;
+      if constexpr (C::EB == 4) {
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t regs[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) regs[i] = f32_to_tf32_rna(s[c * 32 + i]);
+          tmem_st32(s_addr + c * 32, regs);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < BN / 64; ++c) {
+          uint32_t regs[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            if constexpr (kFmt == 1)
+              regs[i] = pack_bf16x2(s[c * 64 + 2 * i], s[c * 64 + 2 * i + 1]);
+            else
+              regs[i] = pack_f16x2(s[c * 64 + 2 * i], s[c * 64 + 2 * i + 1]);
+          }
+          tmem_st32(s_addr + c * 32, regs);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&p_full[k]);
+    }
+    // ------------------------------ epilogue ------------------------------
+    if (n > 0 && ok) ok = mbar_wait(&o_full[k], 0, abort_flag, limit, 9);
+    if (n > 0 && ok) {
+      tc_fence_after();
+      const float inv_l = l > 0.f ? 1.f / l : 0.f;
+      const bool row_ok = q_local < p.Tq;
+      const size_t row_index = (size_t)bh * p.q_rows_alloc + p.q_row0 + q_local;
+      DT* orow = reinterpret_cast<DT*>(p.o) + row_index * HD;
+#pragma unroll
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t regs[32];
+        tmem_ld32(o_addr + c * 32, regs);
+        tmem_wait_ld();
+        if (row_ok) {
+          if constexpr (C::EB == 4) {
+            float4* dst = reinterpret_cast<float4*>(orow + c * 32);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              dst[i] = make_float4(__uint_as_float(regs[4 * i]) * inv_l, __uint_as_float(regs[4 * i + 1]) * inv_l,
+                                   __uint_as_float(regs[4 * i + 2]) * inv_l,
+                                   __uint_as_float(regs[4 * i + 3]) * inv_l);
+          } else {
+            uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              uint32_t w[4];
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                const float a = __uint_as_float(regs[8 * i + 2 * h]) * inv_l;
+                const float b = __uint_as_float(regs[8 * i + 2 * h + 1]) * inv_l;
+                w[h] = (kFmt == 1) ? pack_bf16x2(a, b) : pack_f16x2(a, b);
+              }
+              dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          }
+        }
+      }
+      if (row_ok && p.lse != nullptr) {
+        const float m_use = (m == -INFINITY) ? 0.f : m;
+        p.lse[row_index] = l > 0.f ? (m_use + __log2f(l)) * 0.69314718055994531f : -INFINITY;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == MMA_WARP) {
+    tc_fence_after();
+    tmem_dealloc(tbase, C::TMEM_COLS);
+  }
+}
+
+}  // namespace ctfa

@@ -1,0 +1,439 @@
+// extern "C" entry points of libctfa_b200.so (declared in include/ctfa.h).
+//
+// Host side of the attention path: argument checks, TMA tensor-map encoding,
+// kernel selection (compile-time element type x head dim), launches.  All
+// launches go to the caller's stream; nothing here allocates device memory or
+// synchronises, except ctfa_check_device_error / ctfa_selftest_wait_timeout.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/ctfa.h"
+#include "attn_bwd_sm100.cuh"
+#include "attn_fwd_sm100.cuh"
+#include "attn_simt.cuh"
+
+using namespace ctfa;
+
+namespace {
+
+constexpr int kVersion = 10000;  // 1.0.0
+unsigned long long g_wait_limit_ns = 2000000000ull;
+thread_local std::string g_last_error;
+
+int fail(int status, const std::string& msg) {
+  g_last_error = msg;
+  return status;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  return fail(CTFA_ERR_CUDA, std::string(where) + ": " + cudaGetErrorString(e));
+}
+
+size_t dtype_bytes(int dtype) {
+  switch (dtype) {
+    case CTFA_DTYPE_F32: return 4;
+    case CTFA_DTYPE_BF16: return 2;
+    case CTFA_DTYPE_F16: return 2;
+    case CTFA_DTYPE_F64: return 8;
+    default: return 0;
+  }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---------------------------------------------------------------------------
+// Tensor maps (driver entry point fetched through the runtime, no -lcuda)
+// ---------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// 3-D map over an allocation [BH][rows][D] with a (128-byte x box_rows x 1)
+// box and 128-byte swizzle.  Rows past `rows` read as zero.
+int make_map(CUtensorMap* map, const void* base, int dtype, int D, int rows, int BH, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return fail(CTFA_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  const size_t eb = dtype_bytes(dtype);
+  CUtensorMapDataType dt = dtype == CTFA_DTYPE_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                           : dtype == CTFA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)rows, (cuuint64_t)BH};
+  cuuint64_t strides[2] = {(cuuint64_t)D * eb, (cuuint64_t)rows * D * eb};
+  cuuint32_t box[3] = {(cuuint32_t)(128 / eb), (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(CTFA_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return CTFA_OK;
+}
+
+int device_is_sm100(bool* yes) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  *yes = (major == 10 && minor == 0);
+  return CTFA_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Problem description shared by the full-sequence and block entry points.
+// ---------------------------------------------------------------------------
+struct Problem {
+  int B, H, D, dtype;
+  int Tq, Tk;
+  int q_rows, k_rows;  // rows per head in the allocations
+  int q_row0, k_row0;
+  int causal, causal_offset;
+};
+
+bool tensor_core_shape(const Problem& pr) {
+  return (pr.dtype == CTFA_DTYPE_F32 || pr.dtype == CTFA_DTYPE_BF16 || pr.dtype == CTFA_DTYPE_F16) &&
+         (pr.D == 64 || pr.D == 128);
+}
+
+template <typename DT, int HD, int NQ, int BN, int ST>
+int launch_fwd_tc(const Problem& pr, const void* q, const void* k, const void* v, void* o, float* lse,
+                  cudaStream_t stream) {
+  using C = FwdConfig<DT, HD, NQ, BN, ST>;
+  CUtensorMap mq, mk, mv;
+  int s;
+  if ((s = make_map(&mq, q, pr.dtype, HD, pr.q_rows, pr.B * pr.H, 128)) != CTFA_OK) return s;
+  if ((s = make_map(&mk, k, pr.dtype, HD, pr.k_rows, pr.B * pr.H, BN)) != CTFA_OK) return s;
+  if ((s = make_map(&mv, v, pr.dtype, HD, pr.k_rows, pr.B * pr.H, BN)) != CTFA_OK) return s;
+  FwdParams p;
+  p.BH = pr.B * pr.H;
+  p.Tq = pr.Tq;
+  p.Tk = pr.Tk;
+  p.q_row0 = pr.q_row0;
+  p.k_row0 = pr.k_row0;
+  p.q_rows_alloc = pr.q_rows;
+  p.causal = pr.causal;
+  p.causal_offset = pr.causal_offset;
+  const int q_tiles = (pr.Tq + 127) / 128;
+  p.n_groups = (q_tiles + NQ - 1) / NQ;
+  p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)HD));
+  p.o = o;
+  p.lse = lse;
+  p.wait_limit_ns = g_wait_limit_ns;
+  auto kern = attn_fwd_sm100<DT, HD, NQ, BN, ST>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attn_fwd_sm100)");
+  const long long grid = (long long)p.n_groups * p.BH;
+  if (grid > 0x7fffffffLL) return fail(CTFA_ERR_UNSUPPORTED, "grid too large");
+  kern<<<(unsigned)grid, C::THREADS, C::SMEM_BYTES, stream>>>(mq, mk, mv, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch attn_fwd_sm100");
+  return CTFA_OK;
+}
+
+SimtParams simt_params(const Problem& pr) {
+  SimtParams p;
+  p.BH = pr.B * pr.H;
+  p.Tq = pr.Tq;
+  p.Tk = pr.Tk;
+  p.D = pr.D;
+  p.q_row0 = pr.q_row0;
+  p.k_row0 = pr.k_row0;
+  p.q_rows_alloc = pr.q_rows;
+  p.k_rows_alloc = pr.k_rows;
+  p.causal = pr.causal;
+  p.causal_offset = pr.causal_offset;
+  p.scale = 1.0 / std::sqrt((double)pr.D);
+  return p;
+}
+
+unsigned warps_grid(long long warps) { return (unsigned)((warps * 32 + 255) / 256); }
+
+template <typename DT>
+int launch_fwd_simt(const Problem& pr, const void* q, const void* k, const void* v, void* o, float* lse,
+                    cudaStream_t stream) {
+  SimtParams p = simt_params(pr);
+  attn_fwd_simt<DT><<<warps_grid((long long)p.BH * p.Tq), 256, 0, stream>>>(
+      (const DT*)q, (const DT*)k, (const DT*)v, (DT*)o, lse, p);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? CTFA_OK : cuda_fail(e, "launch attn_fwd_simt");
+}
+
+int forward_impl(const Problem& pr, const void* q, const void* k, const void* v, void* o, float* lse,
+                 cudaStream_t stream) {
+  if (tensor_core_shape(pr)) {
+    bool sm100 = false;
+    int s = device_is_sm100(&sm100);
+    if (s != CTFA_OK) return s;
+    if (!sm100) return fail(CTFA_ERR_UNSUPPORTED, "tensor-core attention kernels need an sm_100 (B200) device");
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+      return fail(CTFA_ERR_MISALIGNED, "q/k/v/o must be 16-byte aligned");
+    switch (pr.dtype) {
+      case CTFA_DTYPE_F32:
+        return pr.D == 64 ? launch_fwd_tc<float, 64, 2, 128, 2>(pr, q, k, v, o, lse, stream)
+                          : launch_fwd_tc<float, 128, 1, 64, 2>(pr, q, k, v, o, lse, stream);
+      case CTFA_DTYPE_BF16:
+        return pr.D == 64 ? launch_fwd_tc<__nv_bfloat16, 64, 2, 128, 3>(pr, q, k, v, o, lse, stream)
+                          : launch_fwd_tc<__nv_bfloat16, 128, 2, 128, 2>(pr, q, k, v, o, lse, stream);
+      default:
+        return pr.D == 64 ? launch_fwd_tc<__half, 64, 2, 128, 3>(pr, q, k, v, o, lse, stream)
+                          : launch_fwd_tc<__half, 128, 2, 128, 2>(pr, q, k, v, o, lse, stream);
+    }
+  }
+  switch (pr.dtype) {
+    case CTFA_DTYPE_F32: return launch_fwd_simt<float>(pr, q, k, v, o, lse, stream);
+    case CTFA_DTYPE_BF16: return launch_fwd_simt<__nv_bfloat16>(pr, q, k, v, o, lse, stream);
+    case CTFA_DTYPE_F16: return launch_fwd_simt<__half>(pr, q, k, v, o, lse, stream);
+    default: return launch_fwd_simt<double>(pr, q, k, v, o, lse, stream);
+  }
+}
+
+int check_common(int B, int H, int T, int D, int dtype) {
+  if (B <= 0 || H <= 0 || T <= 0 || D <= 0) return fail(CTFA_ERR_INVALID_ARGUMENT, "B, H, T and D must be positive");
+  if (dtype_bytes(dtype) == 0) return fail(CTFA_ERR_INVALID_ARGUMENT, "unknown dtype");
+  if (D > 256) return fail(CTFA_ERR_UNSUPPORTED, "head dim above 256 is not supported");
+  if ((long long)B * H > 0x7fffffffLL) return fail(CTFA_ERR_UNSUPPORTED, "B*H too large");
+  return CTFA_OK;
+}
+
+Problem full_problem(int B, int H, int T, int D, int dtype, int causal) {
+  Problem pr;
+  pr.B = B;
+  pr.H = H;
+  pr.D = D;
+  pr.dtype = dtype;
+  pr.Tq = pr.Tk = T;
+  pr.q_rows = pr.k_rows = T;
+  pr.q_row0 = pr.k_row0 = 0;
+  pr.causal = causal ? 1 : 0;
+  pr.causal_offset = 0;
+  return pr;
+}
+
+// ---------------------------------------------------------------------------
+// Backward
+// ---------------------------------------------------------------------------
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+size_t bwd_workspace(const Problem& pr) {
+  const size_t rows = (size_t)pr.B * pr.H * pr.Tq;
+  if (tensor_core_shape(pr)) return align256(rows * sizeof(float));  // delta
+  return align256(rows * (pr.dtype == CTFA_DTYPE_F64 ? sizeof(double) : sizeof(float)));
+}
+
+template <typename DT>
+int launch_bwd_simt(const Problem& pr, const void* q, const void* k, const void* v, const void* o, const void* dO,
+                    const float* lse, void* dq, void* dk, void* dv, void* ws, cudaStream_t stream) {
+  using A = AccT<DT>;
+  SimtParams p = simt_params(pr);
+  A* delta = reinterpret_cast<A*>(ws);
+  attn_bwd_delta_simt<DT><<<warps_grid((long long)p.BH * p.Tq), 256, 0, stream>>>((const DT*)o, (const DT*)dO,
+                                                                                   delta, p);
+  attn_bwd_dq_simt<DT><<<warps_grid((long long)p.BH * p.Tq), 256, 0, stream>>>(
+      (const DT*)q, (const DT*)k, (const DT*)v, (const DT*)dO, lse, delta, (DT*)dq, p);
+  attn_bwd_dkdv_simt<DT><<<warps_grid((long long)p.BH * p.Tk), 256, 0, stream>>>(
+      (const DT*)q, (const DT*)k, (const DT*)v, (const DT*)dO, lse, delta, (DT*)dk, (DT*)dv, p);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? CTFA_OK : cuda_fail(e, "launch attn_bwd_simt");
+}
+
+template <typename DT, int HD>
+int launch_bwd_tc(const Problem& pr, const void* q, const void* k, const void* v, const void* o, const void* dO,
+                  const float* lse, void* dq, void* dk, void* dv, void* ws, cudaStream_t stream) {
+  using C = BwdConfig<DT, HD>;
+  const int BH = pr.B * pr.H;
+  float* delta = reinterpret_cast<float*>(ws);
+  // 1. delta = rowsum(O * dO)
+  BwdPrepParams pp;
+  pp.rows = (long long)BH * pr.Tq;
+  pp.Tq = pr.Tq;
+  pp.q_rows_alloc = pr.q_rows;
+  pp.q_row0 = pr.q_row0;
+  pp.o = o;
+  pp.dO = dO;
+  pp.delta = delta;
+  attn_bwd_prep<DT, HD><<<warps_grid(pp.rows), 256, 0, stream>>>(pp);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch attn_bwd_prep");
+  // 2. dK/dV (key-stationary) and dQ (query-stationary)
+  CUtensorMap mq, mk, mv, mdo;
+  int s;
+  if ((s = make_map(&mq, q, pr.dtype, HD, pr.q_rows, BH, C::BM)) != CTFA_OK) return s;
+  if ((s = make_map(&mdo, dO, pr.dtype, HD, pr.q_rows, BH, C::BM)) != CTFA_OK) return s;
+  if ((s = make_map(&mk, k, pr.dtype, HD, pr.k_rows, BH, C::BN)) != CTFA_OK) return s;
+  if ((s = make_map(&mv, v, pr.dtype, HD, pr.k_rows, BH, C::BN)) != CTFA_OK) return s;
+  BwdParams p;
+  p.BH = BH;
+  p.Tq = pr.Tq;
+  p.Tk = pr.Tk;
+  p.q_row0 = pr.q_row0;
+  p.k_row0 = pr.k_row0;
+  p.q_rows_alloc = pr.q_rows;
+  p.k_rows_alloc = pr.k_rows;
+  p.causal = pr.causal;
+  p.causal_offset = pr.causal_offset;
+  p.scale = (float)(1.0 / std::sqrt((double)HD));
+  p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)HD));
+  p.lse = lse;
+  p.delta = delta;
+  p.dq = dq;
+  p.dk = dk;
+  p.dv = dv;
+  p.wait_limit_ns = g_wait_limit_ns;
+  const int n_kt = (pr.Tk + C::BN - 1) / C::BN;
+  const int n_qt = (pr.Tq + C::BM - 1) / C::BM;
+  auto kdkdv = attn_bwd_dkdv_sm100<DT, HD>;
+  e = cudaFuncSetAttribute(kdkdv, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attn_bwd_dkdv_sm100)");
+  kdkdv<<<(unsigned)((long long)n_kt * BH), C::THREADS, C::SMEM_BYTES, stream>>>(mq, mk, mv, mdo, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch attn_bwd_dkdv_sm100");
+  auto kdq = attn_bwd_dq_sm100<DT, HD>;
+  e = cudaFuncSetAttribute(kdq, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attn_bwd_dq_sm100)");
+  kdq<<<(unsigned)((long long)n_qt * BH), C::THREADS, C::SMEM_BYTES, stream>>>(mq, mk, mv, mdo, p, n_qt);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch attn_bwd_dq_sm100");
+  return CTFA_OK;
+}
+
+int backward_impl(const Problem& pr, const void* q, const void* k, const void* v, const void* o, const void* dO,
+                  const float* lse, void* dq, void* dk, void* dv, void* ws, cudaStream_t stream) {
+  if (tensor_core_shape(pr)) {
+    bool sm100 = false;
+    int s = device_is_sm100(&sm100);
+    if (s != CTFA_OK) return s;
+    if (!sm100) return fail(CTFA_ERR_UNSUPPORTED, "tensor-core attention kernels need an sm_100 (B200) device");
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(dO) || !aligned16(dq) ||
+        !aligned16(dk) || !aligned16(dv))
+      return fail(CTFA_ERR_MISALIGNED, "q/k/v/o/dO/dq/dk/dv must be 16-byte aligned");
+    switch (pr.dtype) {
+      case CTFA_DTYPE_F32:
+        if (pr.D == 64) return launch_bwd_tc<float, 64>(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, stream);
+        break;  // fp32 D=128 does not fit the tensor-core backward's shared memory: SIMT below
+      case CTFA_DTYPE_BF16:
+        return pr.D == 64 ? launch_bwd_tc<__nv_bfloat16, 64>(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, stream)
+                          : launch_bwd_tc<__nv_bfloat16, 128>(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, stream);
+      default:
+        return pr.D == 64 ? launch_bwd_tc<__half, 64>(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, stream)
+                          : launch_bwd_tc<__half, 128>(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, stream);
+    }
+  }
+  switch (pr.dtype) {
+    case CTFA_DTYPE_F32: return launch_bwd_simt<float>(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, stream);
+    case CTFA_DTYPE_BF16: return launch_bwd_simt<__nv_bfloat16>(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, stream);
+    case CTFA_DTYPE_F16: return launch_bwd_simt<__half>(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, stream);
+    default: return launch_bwd_simt<double>(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, stream);
+  }
+}
+
+// One CTA waits on an mbarrier that nothing arrives on.
+__global__ void selftest_wait_kernel(unsigned long long limit_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(&bar, 0, &abort_flag, limit_ns, 100);
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// extern "C"
+// ---------------------------------------------------------------------------
+extern "C" int ctfa_version(void) { return kVersion; }
+
+extern "C" const char* ctfa_status_string(int status) {
+  switch (status) {
+    case CTFA_OK: return "CTFA_OK";
+    case CTFA_ERR_INVALID_ARGUMENT: return "CTFA_ERR_INVALID_ARGUMENT";
+    case CTFA_ERR_UNSUPPORTED: return "CTFA_ERR_UNSUPPORTED";
+    case CTFA_ERR_MISALIGNED: return "CTFA_ERR_MISALIGNED";
+    case CTFA_ERR_CUDA: return "CTFA_ERR_CUDA";
+    case CTFA_ERR_DEVICE_TIMEOUT: return "CTFA_ERR_DEVICE_TIMEOUT";
+    case CTFA_ERR_WORKSPACE: return "CTFA_ERR_WORKSPACE";
+    default: return "CTFA_ERR_UNKNOWN";
+  }
+}
+
+extern "C" const char* ctfa_last_error_message(void) { return g_last_error.c_str(); }
+
+extern "C" int ctfa_set_wait_limit_ns(unsigned long long ns) {
+  if (ns == 0) return fail(CTFA_ERR_INVALID_ARGUMENT, "wait limit must be positive");
+  g_wait_limit_ns = ns;
+  return CTFA_OK;
+}
+
+extern "C" int ctfa_forward(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H, int T,
+                            int D, int dtype, int causal, void* stream) {
+  int s = check_common(B, H, T, D, dtype);
+  if (s != CTFA_OK) return s;
+  if (!q || !k || !v || !o) return fail(CTFA_ERR_INVALID_ARGUMENT, "q, k, v and o must be non-null");
+  return forward_impl(full_problem(B, H, T, D, dtype, causal), q, k, v, o, lse, (cudaStream_t)stream);
+}
+
+extern "C" size_t ctfa_backward_workspace_bytes(int B, int H, int T, int D, int dtype) {
+  if (check_common(B, H, T, D, dtype) != CTFA_OK) return 0;
+  return bwd_workspace(full_problem(B, H, T, D, dtype, 0));
+}
+
+extern "C" int ctfa_backward(const void* q, const void* k, const void* v, const void* o, const void* dO,
+                             const float* lse, void* dq, void* dk, void* dv, void* workspace,
+                             size_t workspace_bytes, int B, int H, int T, int D, int dtype, int causal,
+                             void* stream) {
+  int s = check_common(B, H, T, D, dtype);
+  if (s != CTFA_OK) return s;
+  if (!q || !k || !v || !o || !dO || !lse || !dq || !dk || !dv)
+    return fail(CTFA_ERR_INVALID_ARGUMENT, "q, k, v, o, dO, lse, dq, dk and dv must be non-null");
+  Problem pr = full_problem(B, H, T, D, dtype, causal);
+  const size_t need = bwd_workspace(pr);
+  if (!workspace || workspace_bytes < need)
+    return fail(CTFA_ERR_WORKSPACE, "workspace needs " + std::to_string(need) + " bytes");
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return fail(CTFA_ERR_MISALIGNED, "workspace must be 256-byte aligned");
+  return backward_impl(pr, q, k, v, o, dO, lse, dq, dk, dv, workspace, (cudaStream_t)stream);
+}
+
+extern "C" int ctfa_check_device_error(void* stream) {
+  cudaError_t e = cudaStreamSynchronize((cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  DeviceError err;
+  e = cudaMemcpyFromSymbol(&err, g_device_error, sizeof(err));
+  if (e != cudaSuccess) return cuda_fail(e, "read device error word");
+  if (err.code != 0) {
+    DeviceError zero = {0, 0, 0, 0};
+    cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero));
+    char buf[160];
+    snprintf(buf, sizeof(buf), "kernel wait gave up (site %d, block %d, thread %d)", err.site, err.block,
+             err.thread);
+    return fail(CTFA_ERR_DEVICE_TIMEOUT, buf);
+  }
+  return CTFA_OK;
+}
+
+extern "C" int ctfa_selftest_wait_timeout(unsigned long long limit_ns, void* stream) {
+  if (limit_ns == 0 || limit_ns > 10000000000ull)
+    return fail(CTFA_ERR_INVALID_ARGUMENT, "limit must be in (0, 10 s]");
+  selftest_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(limit_ns);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch selftest_wait_kernel");
+  return ctfa_check_device_error(stream);
+}

@@ -1,0 +1,110 @@
+/*
+ * ctfa.h -- C ABI of the B200 (sm_100a) flash-attention library
+ * (libctfa_b200.so).
+ *
+ * These entry points are the seam under CudaTransformer's
+ * FlashAttentionLayer<DType> (cuda_transformer/FlashAttentionLayer.cu).  The
+ * layer keeps its C++ API; its two kernel launches become calls into this
+ * library.  Every function takes plain device pointers, sizes and a CUDA
+ * stream (cudaStream_t passed as void*; NULL = legacy default stream, which
+ * is what the reference launches on), returns a status code, and never
+ * allocates or synchronises unless stated.
+ *
+ * Tensor layout (unchanged from the reference, Tensor<DType> contiguous
+ * row-major, cuda_transformer/Tensor.cu:10-170):
+ *   q, k, v, o, dO, dq, dk, dv : [B, H, T, D], D fastest
+ *   lse                        : [B, H, T] float32, natural-log logsumexp
+ *                                of the scaled scores of each query row
+ * Softmax scale: 1/sqrt(D) (flash_attention.cu:116).
+ */
+#ifndef CTFA_H_
+#define CTFA_H_
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define CTFA_OK 0
+#define CTFA_ERR_INVALID_ARGUMENT 1 /* null pointer, non-positive size, bad dtype */
+#define CTFA_ERR_UNSUPPORTED 2      /* shape / dtype / device the library cannot run */
+#define CTFA_ERR_MISALIGNED 3       /* tensor-core path needs 16-byte aligned tensors */
+#define CTFA_ERR_CUDA 4             /* a CUDA runtime call or launch failed */
+#define CTFA_ERR_DEVICE_TIMEOUT 5   /* a kernel gave up on a bounded wait */
+#define CTFA_ERR_WORKSPACE 6        /* workspace missing or too small */
+
+/* Element types of q/k/v/o/dO/dq/dk/dv (the DType template argument of the
+ * reference layer: float, __nv_bfloat16, __half, double). */
+#define CTFA_DTYPE_F32 0  /* fp32 I/O, tcgen05 kind::tf32, fp32 softmax/accumulation */
+#define CTFA_DTYPE_BF16 1 /* bf16 I/O, tcgen05 kind::f16, fp32 softmax/accumulation */
+#define CTFA_DTYPE_F16 2  /* fp16 I/O, tcgen05 kind::f16, fp32 softmax/accumulation */
+#define CTFA_DTYPE_F64 3  /* fp64 I/O, SIMT fp64 kernels */
+
+/* Library version: major*10000 + minor*100 + patch. */
+int ctfa_version(void);
+
+/* Human-readable name of a status code. */
+const char* ctfa_status_string(int status);
+
+/* Detail message of the last failing call made by this host thread. */
+const char* ctfa_last_error_message(void);
+
+/*
+ * Forward: o = softmax(q k^T / sqrt(D) [+ causal mask]) v, lse per row.
+ * Replaces the launch of flashAttention<DType> in
+ * FlashAttentionLayer::computeAttention (FlashAttentionLayer.cu:45-87, kernel
+ * at flash_attention.cu:57-169).  causal = 0 reproduces the reference's
+ * semantics (every query attends every key); causal = 1 masks key j > query i.
+ * lse may be NULL when the caller does not keep it for the backward pass.
+ * D: any value in [1, 256]; D = 64 and D = 128 with f32/bf16/f16 run on the
+ * tcgen05 tensor-core kernels, everything else on SIMT kernels.
+ */
+int ctfa_forward(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H, int T, int D,
+                 int dtype, int causal, void* stream);
+
+/* Bytes of device workspace ctfa_backward needs for this problem. */
+size_t ctfa_backward_workspace_bytes(int B, int H, int T, int D, int dtype);
+
+/*
+ * Backward: dq, dk, dv from q, k, v, the forward output o, its gradient dO and
+ * the forward's lse.  Replaces the launch of flashAttentionBackward<DType> in
+ * FlashAttentionLayer::computeBackward (FlashAttentionLayer.cu:97-142, kernel
+ * at flash_attention.cu:226-326).  Unlike the reference, dk and dv are the
+ * exact gradients (the reference kernel mixes the query index into the key
+ * rows it updates, flash_attention.cu:310-321).  dq/dk/dv are fully written
+ * (no zero-filled inputs required).  workspace: device memory of at least
+ * ctfa_backward_workspace_bytes(...) bytes, 256-byte aligned.
+ */
+int ctfa_backward(const void* q, const void* k, const void* v, const void* o, const void* dO, const float* lse,
+                  void* dq, void* dk, void* dv, void* workspace, size_t workspace_bytes, int B, int H, int T,
+                  int D, int dtype, int causal, void* stream);
+
+/*
+ * Bound, in nanoseconds, on every wait inside the kernels (default 2e9).  A
+ * kernel that waits longer records CTFA_ERR_DEVICE_TIMEOUT in a device error
+ * word and exits without touching its outputs further.
+ */
+int ctfa_set_wait_limit_ns(unsigned long long ns);
+
+/*
+ * Synchronise `stream`, then read and clear the device error word.  Returns
+ * CTFA_OK, CTFA_ERR_DEVICE_TIMEOUT (a kernel gave up on a wait) or
+ * CTFA_ERR_CUDA (an asynchronous CUDA error).
+ */
+int ctfa_check_device_error(void* stream);
+
+/*
+ * Self-test of the bounded-wait path: launches one CTA that waits on an
+ * mbarrier nothing arrives on, with the given limit, then checks the device
+ * error word.  Returns CTFA_ERR_DEVICE_TIMEOUT when the wait gave up as
+ * designed (the expected result), CTFA_OK if it did not.
+ */
+int ctfa_selftest_wait_timeout(unsigned long long limit_ns, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CTFA_H_ */

@@ -1,0 +1,71 @@
+"""CPU: the C-ABI library loads, exports every symbol include/ctfa.h declares,
+and rejects bad arguments on the host before any CUDA call."""
+import ctypes
+import re
+
+import pytest
+
+from cudatransformer_b200 import _lib
+
+
+def declared_functions():
+    text = _lib.HEADER_PATH.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(ctfa_\w+)\s*\(", text)))
+
+
+def test_header_declares_the_entry_points():
+    names = declared_functions()
+    for required in ("ctfa_forward", "ctfa_backward", "ctfa_backward_workspace_bytes", "ctfa_version"):
+        assert required in names
+
+
+def test_every_declared_symbol_is_exported(ctfa):
+    for name in declared_functions():
+        assert hasattr(ctfa, name), f"{name} declared in include/ctfa.h but not exported"
+
+
+def test_binding_table_matches_header():
+    assert set(_lib.SIGNATURES) == set(declared_functions())
+
+
+def test_version_and_status_strings(ctfa):
+    assert ctfa.ctfa_version() >= 10000
+    for code in range(7):
+        assert ctfa.ctfa_status_string(code).decode().startswith("CTFA_")
+
+
+FAKE = ctypes.c_void_p(4096)  # never dereferenced: every call below fails validation first
+
+
+@pytest.mark.parametrize(
+    "args,status",
+    [
+        ((None, FAKE, FAKE, FAKE, None, 1, 1, 8, 64, 0, 0, None), _lib.CTFA_ERR_INVALID_ARGUMENT),
+        ((FAKE, FAKE, FAKE, FAKE, None, 0, 1, 8, 64, 0, 0, None), _lib.CTFA_ERR_INVALID_ARGUMENT),
+        ((FAKE, FAKE, FAKE, FAKE, None, 1, 1, -3, 64, 0, 0, None), _lib.CTFA_ERR_INVALID_ARGUMENT),
+        ((FAKE, FAKE, FAKE, FAKE, None, 1, 1, 8, 64, 7, 0, None), _lib.CTFA_ERR_INVALID_ARGUMENT),
+        ((FAKE, FAKE, FAKE, FAKE, None, 1, 1, 8, 300, 0, 0, None), _lib.CTFA_ERR_UNSUPPORTED),
+    ],
+)
+def test_forward_argument_validation(ctfa, args, status):
+    assert ctfa.ctfa_forward(*args) == status
+    assert _lib.last_error()
+
+
+def test_backward_argument_validation(ctfa):
+    ws = ctfa.ctfa_backward_workspace_bytes(2, 3, 100, 64, _lib.CTFA_DTYPE_BF16)
+    assert ws >= 2 * 3 * 100 * 4 and ws % 256 == 0
+    args = [FAKE] * 9 + [None, 0, 2, 3, 100, 64, _lib.CTFA_DTYPE_BF16, 1, None]
+    assert ctfa.ctfa_backward(*args) == _lib.CTFA_ERR_WORKSPACE
+    args[5] = None  # lse
+    assert ctfa.ctfa_backward(*args) == _lib.CTFA_ERR_INVALID_ARGUMENT
+    args = [FAKE] * 9 + [ctypes.c_void_p(4096 + 8), ws, 2, 3, 100, 64, _lib.CTFA_DTYPE_BF16, 1, None]
+    assert ctfa.ctfa_backward(*args) == _lib.CTFA_ERR_MISALIGNED  # workspace not 256-byte aligned
+    assert ctfa.ctfa_backward_workspace_bytes(0, 1, 1, 64, 0) == 0
+
+
+def test_wait_limit_validation(ctfa):
+    assert ctfa.ctfa_set_wait_limit_ns(0) == _lib.CTFA_ERR_INVALID_ARGUMENT
+    assert ctfa.ctfa_set_wait_limit_ns(2_000_000_000) == _lib.CTFA_OK
+    assert ctfa.ctfa_selftest_wait_timeout(0, None) == _lib.CTFA_ERR_INVALID_ARGUMENT
