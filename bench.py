@@ -1,0 +1,474 @@
+#!/usr/bin/env python
+"""Benchmark of the attention hot path: causal flash-attention forward +
+backward through libctfa_b200.so (C ABI, tcgen05 kernels).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload config2|config3]
+
+One step = forward (o, lse) + backward (dq, dk, dv) of one batch.  Default
+workload = BASELINE config 2 (GPT-2-small attention: B=8 per GPU, H=12,
+T=1024, D=64, fp32 I/O through tf32 MMAs, causal).  With N GPUs (torchrun,
+one rank per GPU) every rank owns its own 8 sequences (batch x head shards,
+no collective in the step): weak scaling, value = all ranks' FLOPs / max time.
+
+FLOP convention (algorithmic): causal fwd + bwd = 7 * B*H*T^2*D
+(2 GEMMs forward + 5 backward, each half-masked); non-causal = 14 * B*H*T^2*D.
+
+Printed JSON line (rank 0): value = device-resident throughput (inputs in HBM
+when the timed region starts); e2e = same metric through the C ABI with
+pinned host buffers, H2D of q/k/v/dO and D2H of o/dq/dk/dv inside the timed
+region; roofline for the dominant kernel, timed with CUDA events on its own
+launch stream; cpu_baseline = the fp32 OpenMP CPU attention (oracle) on a
+bounded sample of heads, on this host.
+
+--impl reference times the reference's own CUDA FlashAttentionLayer<float>
+(computeAttention(saveStates=true) + computeBackward + clearCache, compiled
+unmodified from its sources into oracle/_ref/libctref.so) on one GPU, on the
+same shape.  The reference has no causal mask, so it computes the full
+(non-causal) attention; its FLOPs are counted at 14 * B*H*T^2*D, the work it
+does.  Under torchrun only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "causal attention fwd+bwd TFLOP/s and % of B200 tensor peak at 1/2/4/8 GPUs"
+
+WORKLOADS = {
+    "config2": dict(desc="BASELINE config 2: GPT-2-small attention shape", B=8, H=12, T=1024, D=64, dtype="f32",
+                    causal=True, qkv_scale=0.5, do_scale=1.0, seed=1),
+    "config3": dict(desc="BASELINE config 3: bf16 I/O, D=128", B=16, H=16, T=2048, D=128, dtype="bf16",
+                    causal=True, qkv_scale=1.0, do_scale=0.1, seed=2),
+}
+
+
+def path_flops(B, H, T, D, causal):
+    return (7 if causal else 14) * B * H * T * T * D
+
+
+def gemm_flops(B, H, T, D, causal):
+    """One T x T x D GEMM per head, halved under the causal mask."""
+    return (1 if causal else 2) * B * H * T * T * D
+
+
+def measured_peaks():
+    try:
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except Exception:
+        return {}
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled with nvidia-smi during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.tmp, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.tmp.flush()
+        rows = []
+        for line in Path(self.tmp.name).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 10:
+                continue
+            try:
+                rows.append(dict(sm=float(parts[1]), smax=float(parts[2]), power=float(parts[3]),
+                                 util=float(parts[4]), hw=parts[6], hwt=parts[7], swt=parts[8], pcap=parts[9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        loaded = [r for r in rows if r["util"] >= 50] or rows
+        reasons = sorted({name for r in loaded for name, key in
+                          (("hw_slowdown", "hw"), ("hw_thermal_slowdown", "hwt"), ("sw_thermal_slowdown", "swt"),
+                           ("sw_power_cap", "pcap")) if r[key].lower() == "active"})
+        return {"sm_mhz": statistics.median(r["sm"] for r in loaded), "sm_max_mhz": max(r["smax"] for r in rows),
+                "power_w_max": max(r["power"] for r in rows), "samples": len(rows),
+                "samples_under_load": len(loaded), "reasons": reasons}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+def dist_init(n_gpus):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# our implementation
+# ---------------------------------------------------------------------------
+def tf32_peak_tflops():
+    """cuBLAS tf32 GEMM 8192^3, best of 10 (the denominator for fp32 I/O)."""
+    import torch
+
+    torch.backends.cuda.matmul.allow_tf32 = True
+    n = 8192
+    a = torch.randn(n, n, device="cuda")
+    b = torch.randn(n, n, device="cuda")
+    for _ in range(3):
+        a @ b
+    best = 0.0
+    for _ in range(10):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        a @ b
+        e.record()
+        e.synchronize()
+        best = max(best, 2 * n ** 3 / (s.elapsed_time(e) * 1e-3) / 1e12)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    del a, b
+    return best
+
+
+def cpu_baseline(w):
+    """fp32 OpenMP CPU attention (oracle/liboracle.so) on a bounded sample of heads."""
+    import numpy as np
+
+    from oracle import oracle as orc
+
+    cores = os.cpu_count() or 1
+    n_heads = min(w["B"] * w["H"], max(8, cores))
+    rng = np.random.default_rng(w["seed"])
+    shape = (1, n_heads, w["T"], w["D"])
+    q, k, v = (rng.standard_normal(shape, dtype=np.float32) * w["qkv_scale"] for _ in range(3))
+    do = rng.standard_normal(shape, dtype=np.float32) * w["do_scale"]
+    t0 = time.perf_counter()
+    orc.cpu_attention_fwd_bwd_f32(q, k, v, do, w["causal"], threads=cores)
+    dt = time.perf_counter() - t0
+    flops = path_flops(1, n_heads, w["T"], w["D"], w["causal"])
+    return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+            "sample": f"{n_heads} of {w['B'] * w['H']} (batch, head) problems of the workload, fp32, "
+                      f"fwd+bwd, {dt:.2f} s wall", "seconds": dt}
+
+
+def run_ours(args, w):
+    import torch
+
+    from cudatransformer_b200 import _lib
+
+    rank, world, local = dist_init(args.gpus)
+    lib = _lib.load()
+    B, H, T, D = w["B"], w["H"], w["T"], w["D"]
+    tdt = {"f32": torch.float32, "bf16": torch.bfloat16}[w["dtype"]]
+    code = {"f32": _lib.CTFA_DTYPE_F32, "bf16": _lib.CTFA_DTYPE_BF16}[w["dtype"]]
+    causal = int(w["causal"])
+    dev = torch.device("cuda", local)
+    gen = torch.Generator().manual_seed(w["seed"] * 1000 + rank)
+    shape = (B, H, T, D)
+
+    def host(scale):
+        return (torch.randn(shape, generator=gen) * scale).to(tdt).pin_memory()
+
+    q_h, k_h, v_h = (host(w["qkv_scale"]) for _ in range(3))
+    do_h = host(w["do_scale"])
+    q, k, v, do = (x.to(dev) for x in (q_h, k_h, v_h, do_h))
+    o, dq, dk, dv = (torch.empty(shape, dtype=tdt, device=dev) for _ in range(4))
+    o_h, dq_h, dk_h, dv_h = (torch.empty(shape, dtype=tdt).pin_memory() for _ in range(4))
+    lse = torch.empty((B, H, T), dtype=torch.float32, device=dev)
+    ws = torch.empty(lib.ctfa_backward_workspace_bytes(B, H, T, D, code), dtype=torch.uint8, device=dev)
+    fws_bytes = lib.ctfa_forward_workspace_bytes(B, H, T, D, code)
+    fws = torch.empty(max(fws_bytes, 256), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sh = stream.cuda_stream
+
+    def fwd():
+        _lib.check(lib.ctfa_forward(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
+                                    B, H, T, D, code, causal, fws.data_ptr(), fws.numel(), sh), "ctfa_forward")
+
+    def bwd(events=None):
+        ptrs = (q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(), lse.data_ptr(),
+                dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), ws.data_ptr(), ws.numel(), B, H, T, D, code, causal, sh)
+        if events is None:
+            _lib.check(lib.ctfa_backward(*ptrs), "ctfa_backward")
+        else:
+            import ctypes
+
+            for ev_ in events:  # torch creates the CUDA event lazily, on first record
+                ev_.record(stream)
+            arr = (ctypes.c_void_p * 4)(*[ev_.cuda_event for ev_ in events])
+            _lib.check(lib.ctfa_backward_with_events(*ptrs, arr), "ctfa_backward_with_events")
+
+    def step():
+        fwd()
+        bwd()
+
+    def e2e_step():
+        for dst, src in ((q, q_h), (k, k_h), (v, v_h), (do, do_h)):
+            dst.copy_(src, non_blocking=True)
+        step()
+        for dst, src in ((o_h, o), (dq_h, dq), (dk_h, dk), (dv_h, dv)):
+            dst.copy_(src, non_blocking=True)
+
+    def timed(fn, steps):
+        barrier(world)
+        torch.cuda.synchronize(dev)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        for _ in range(steps):
+            fn()
+        e.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        return max_over_ranks(s.elapsed_time(e), world)
+
+    for _ in range(args.warmup):
+        step()
+    _lib.check(lib.ctfa_check_device_error(sh), "warm-up (device)")
+    with ClockSampler(local) as clocks:
+        ms = timed(step, args.steps)
+    _lib.check(lib.ctfa_check_device_error(sh), "timed steps (device)")
+    clk = clocks.summary()
+
+    for _ in range(args.warmup):
+        e2e_step()
+    ms_e2e = timed(e2e_step, args.steps)
+
+    # per-kernel durations (events recorded on the launch stream around each launch)
+    names = ("attn_fwd_sm100", "attn_bwd_prep", "attn_bwd_dkdv_sm100", "attn_bwd_dq_sm100")
+    acc = {n: 0.0 for n in names}
+    for _ in range(args.steps):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+        ev[0].record(stream)
+        fwd()
+        ev[1].record(stream)
+        bwd(events=ev[2:6])
+        torch.cuda.synchronize(dev)
+        acc[names[0]] += ev[0].elapsed_time(ev[1])
+        acc[names[1]] += ev[2].elapsed_time(ev[3])
+        acc[names[2]] += ev[3].elapsed_time(ev[4])
+        acc[names[3]] += ev[4].elapsed_time(ev[5])
+    per = {n: acc[n] / args.steps for n in names}
+
+    peaks = measured_peaks()
+    if w["dtype"] == "f32":
+        peak = tf32_peak_tflops() if rank == 0 else 0.0
+        peak_note = "tf32 dense, cuBLAS 8192^3 measured in this run (best of 10)"
+    else:
+        peak = float(peaks.get("bf16_tflops", 1590.0))
+        peak_note = "bf16 dense burst, MEASURED_PEAKS.json" if peaks else "bf16 dense, fallback 1.59 PF"
+    bf16_peak = float(peaks.get("bf16_tflops", 1590.0))
+
+    if rank != 0:
+        barrier(world)
+        return
+    g = gemm_flops(B, H, T, D, w["causal"])
+    kflops = {names[0]: 2 * g, names[1]: 0, names[2]: 4 * g, names[3]: 3 * g}
+    total = path_flops(B, H, T, D, w["causal"])
+    value = world * total / (ms / args.steps * 1e-3) / 1e12
+    e2e_value = world * total / (ms_e2e / args.steps * 1e-3) / 1e12
+    dom = max((n for n in names if kflops[n] > 0), key=lambda n: per[n])
+    achieved = kflops[dom] / (per[dom] * 1e-3) / 1e12
+    traffic = None
+    tpath = ROOT / "profiles" / "roofline_traffic.json"
+    if tpath.exists():
+        try:
+            tj = json.loads(tpath.read_text())
+            entry = tj.get(f"{args.workload}/{dom}")
+            if entry:
+                traffic = entry["dram_bytes_per_launch"]
+        except Exception:
+            traffic = None
+    kernel_table = {n: {"ms": round(per[n], 4), "share": round(per[n] / sum(per.values()), 3),
+                        "tflops": round(kflops[n] / (per[n] * 1e-3) / 1e12, 1) if kflops[n] else None}
+                    for n in names}
+    eb = {"f32": 4, "bf16": 2}[w["dtype"]]
+    nbytes = B * H * T * D * eb
+    cpu = cpu_baseline(w) if world == 1 else None
+    out = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp32 I/O, tf32 tcgen05 MMA" if w["dtype"] == "f32" else "bf16 I/O, bf16 tcgen05 MMA",
+        "data": f"synthetic: q,k,v ~ {w['qkv_scale']}*N(0,1), dO ~ {w['do_scale']}*N(0,1), seeded per rank",
+        "config": {"workload": w["desc"], "batch_per_gpu": B, "global_batch": B * world, "heads": H, "seq_len": T,
+                   "head_dim": D, "causal": w["causal"],
+                   "parallelism": f"batch x head shards over {world} GPU(s), no collective in the step",
+                   "l2": f"working set {9 * nbytes / 1e6:.0f} MB per GPU > 126 MB L2; no flush"},
+        "pct_of_tensor_peak": {"of_dtype_peak": round(100 * value / world / peak, 1) if peak else None,
+                               "dtype_peak_tflops": round(peak, 1), "dtype_peak_source": peak_note,
+                               "of_bf16_dense_peak": round(100 * value / world / bf16_peak, 1)},
+        "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": 4 * nbytes,
+                "d2h_bytes_per_step": 4 * nbytes, "ms_per_step": round(ms_e2e / args.steps, 4),
+                "path": "ctfa_forward + ctfa_backward (C ABI) with pinned host buffers"},
+        "gpu_launches": 4 * args.steps,
+        "roofline": {"kernel": dom, "bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1),
+                     "unit": "TFLOP/s", "frac": round(achieved / peak, 3) if peak else None,
+                     "peak_source": peak_note, "flops_per_launch": kflops[dom],
+                     "traffic": traffic},
+        "kernels": kernel_table,
+        "cpu_baseline": cpu,
+        "clocks": clk,
+    }
+    print(json.dumps(out), flush=True)
+    barrier(world)
+
+
+# ---------------------------------------------------------------------------
+# reference arm
+# ---------------------------------------------------------------------------
+def run_reference(args, w):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import oracle as orc
+
+    lib = orc.load_reference_cuda()
+    if lib is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libctref.so was not built "
+                          "(needs the reference tree at build time)"}))
+        return
+    import torch
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    B, H, T, D = w["B"], w["H"], w["T"], w["D"]
+    if w["dtype"] != "f32":
+        print(json.dumps({"impl": "reference", "unavailable": "bench reference arm runs the fp32 workload only"}))
+        return
+    gen = torch.Generator().manual_seed(w["seed"] * 1000)
+    shape = (B, H, T, D)
+    q, k, v = ((torch.randn(shape, generator=gen) * w["qkv_scale"]).to(dev) for _ in range(3))
+    do = (torch.randn(shape, generator=gen) * w["do_scale"]).to(dev)
+
+    def step():
+        rc = lib.ctref_forward_backward(0, q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(), None, None,
+                                        None, None, B, H, T, D)
+        if rc != 0:
+            raise RuntimeError(f"reference FlashAttentionLayer returned CUDA error {rc}")
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clocks:
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(args.steps):
+            step()
+        e.record()
+        torch.cuda.synchronize(dev)
+    ms = s.elapsed_time(e)
+    flops = path_flops(B, H, T, D, False)  # the reference computes the full (non-causal) attention
+    value = flops / (ms / args.steps * 1e-3) / 1e12
+    out = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 4),
+        "unit": "TFLOP/s",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp32 (SIMT CUDA cores)",
+        "data": "synthetic, same distributions as the ours arm",
+        "config": {"workload": w["desc"], "batch_per_gpu": B, "global_batch": B, "heads": H, "seq_len": T,
+                   "head_dim": D, "causal": False,
+                   "note": "the reference kernel has no causal mask; FLOPs counted at 14*B*H*T^2*D, the work it does"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "kind": "reference", "cores": 0,
+                         "sample": "full workload; the reference's own implementation of this path is CUDA "
+                                   "(FlashAttentionLayer<float> from oracle/_ref), timed on one B200"},
+        "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config2")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    w = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        run_reference(args, w)
+    else:
+        run_ours(args, w)
+
+
+if __name__ == "__main__":
+    main()

@@ -40,12 +40,17 @@ SIGNATURES = {
     "ctfa_forward": (
         _c_int,
         [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
-         _c_void_p],
+         _c_void_p, _c_size_t, _c_void_p],
     ),
+    "ctfa_forward_workspace_bytes": (_c_size_t, [_c_int, _c_int, _c_int, _c_int, _c_int]),
     "ctfa_backward_workspace_bytes": (_c_size_t, [_c_int, _c_int, _c_int, _c_int, _c_int]),
     "ctfa_backward": (
         _c_int,
         [_c_void_p] * 10 + [_c_size_t] + [_c_int] * 6 + [_c_void_p],
+    ),
+    "ctfa_backward_with_events": (
+        _c_int,
+        [_c_void_p] * 10 + [_c_size_t] + [_c_int] * 6 + [_c_void_p, _c_void_p],
     ),
     "ctfa_set_wait_limit_ns": (_c_int, [_c_ull]),
     "ctfa_check_device_error": (_c_int, [_c_void_p]),

@@ -42,6 +42,7 @@ struct BwdPrepParams {
   const void* o;
   const void* dO;
   float* delta;      // [BH][Tq]
+  float* dO_round;   // fp32 I/O only: round-to-nearest tf32 copy of dO (nullable)
 };
 
 struct BwdParams {
@@ -70,7 +71,10 @@ __device__ __forceinline__ float load_as_float(const DT* p) {
     return __half2float(*p);
 }
 
-// One warp per query row: delta = rowsum(O * dO) in fp32.
+// One warp per query row: delta = rowsum(O * dO) in fp32.  For fp32 I/O it
+// also writes the tf32-rounded dO that the MMAs read, and forms delta from
+// that same rounded dO, so that sum_j P_ij dP_ij == delta_i holds for the
+// values the tensor cores see (dS then cancels exactly where it should).
 template <typename DT, int HD>
 __global__ void __launch_bounds__(256) attn_bwd_prep(BwdPrepParams p) {
   const long long w = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -81,55 +85,184 @@ __global__ void __launch_bounds__(256) attn_bwd_prep(BwdPrepParams p) {
   const DT* o = reinterpret_cast<const DT*>(p.o) + row;
   const DT* g = reinterpret_cast<const DT*>(p.dO) + row;
   float s = 0.f;
+  if constexpr (sizeof(DT) == 4) {
+    if (p.dO_round != nullptr) {
+      float* gr = p.dO_round + row;
 #pragma unroll
-  for (int d = lane; d < HD; d += 32) s += load_as_float(o + d) * load_as_float(g + d);
+      for (int d = lane; d < HD; d += 32) {
+        const float r = __uint_as_float(f32_to_tf32_rna(load_as_float(g + d)));
+        gr[d] = r;
+        s += load_as_float(o + d) * r;
+      }
+    } else {
+#pragma unroll
+      for (int d = lane; d < HD; d += 32) s += load_as_float(o + d) * load_as_float(g + d);
+    }
+  } else {
+#pragma unroll
+    for (int d = lane; d < HD; d += 32) s += load_as_float(o + d) * load_as_float(g + d);
+  }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
   if (lane == 0) p.delta[w] = s;
 }
 
+
 template <typename DT, int HD>
 struct BwdConfig {
-  static constexpr int BM = 128;  // query rows per tile
-  static constexpr int BN = 128;  // key rows per tile
   static constexpr int EB = (int)sizeof(DT);
-  static constexpr int E128 = 128 / EB;
-  static constexpr int KBLK = HD * EB / 128;
-  static constexpr int TILE_BYTES = 128 * HD * EB;  // BM == BN == 128
-  static constexpr int KSTEP_S = HD * EB / 32;
-  static constexpr int K_PER = (EB == 4) ? 8 : 16;    // reduction rows per TS MMA
-  static constexpr int KSTEP_T = 128 / K_PER;
   static constexpr bool TF32 = (EB == 4);
-  static constexpr int ST = (TILE_BYTES * 2 * 3 + TILE_BYTES * 2 <= 200 * 1024) ? 3 : 2;  // streamed stages
-  // dK/dV kernel TMEM map (columns)
+  static constexpr int E128 = 128 / EB;
+  static constexpr int KBLK = HD * EB / 128;          // 128-byte column blocks per row
+  static constexpr int KSTEP_S = HD * EB / 32;        // k-steps over the head dim (32 bytes each)
+  static constexpr int K_PER = TF32 ? 8 : 16;         // reduction rows per TS MMA
+  static constexpr int ROW_BYTES = HD * EB;
+  // dK/dV kernel: 128 stationary keys (MMA M); streamed query tiles of KV_QT rows.
+  static constexpr int KV_KEYS = 128;
+  static constexpr int KV_QT = TF32 ? 64 : 128;
+  // dQ kernel: 128 stationary queries; streamed key tiles of Q_KT rows.
+  static constexpr int Q_ROWS = 128;
+  static constexpr int Q_KT = TF32 ? 64 : 128;
+  // tf32 operands read both K-major and MN-major get a second copy in the
+  // 32-byte-granule swizzle; 16-bit operands serve both from one buffer.
+  static constexpr int BIG_TILE = 128 * ROW_BYTES;
+  static constexpr int KV_QTILE = KV_QT * ROW_BYTES;
+  static constexpr int Q_KTILE = Q_KT * ROW_BYTES;
+  static constexpr int KV_STAGE_BYTES = (TF32 ? 4 : 2) * KV_QTILE;  // Q, dO (+ MN copies)
+  static constexpr int Q_STAGE_BYTES = (TF32 ? 3 : 2) * Q_KTILE;    // K, V (+ K MN copy)
+  static constexpr int BUDGET = 216 * 1024;
+  static constexpr int KV_ST = (BUDGET - 2 * BIG_TILE) / KV_STAGE_BYTES > 3 ? 3 : (BUDGET - 2 * BIG_TILE) / KV_STAGE_BYTES;
+  static constexpr int Q_ST = (BUDGET - 2 * BIG_TILE) / Q_STAGE_BYTES > 3 ? 3 : (BUDGET - 2 * BIG_TILE) / Q_STAGE_BYTES;
+  // dK/dV kernel TMEM map (columns, lanes = keys)
+  static constexpr int KV_HALF = KV_QT / 2;  // score columns per compute warpgroup
   static constexpr int KV_S = 0;
-  static constexpr int KV_DP = 128;                       // dP^T, then dS^T (tf32) / dS^T packed (16-bit)
-  static constexpr int KV_P = TF32 ? 256 : 160;           // P^T (tf32) / P^T packed: cols [128+64h+32, +32) per half h
-  static constexpr int KV_DK = TF32 ? 384 : 256;
+  static constexpr int KV_DP = KV_QT;        // dP^T; then dS^T (tf32 in place) or dS^T|P^T packed per half
+  static constexpr int KV_P = TF32 ? 2 * KV_QT : KV_QT + KV_HALF / 2;
+  static constexpr int KV_DK = TF32 ? 3 * KV_QT : 2 * KV_QT;
   static constexpr int KV_DV = KV_DK + HD;
   static constexpr uint32_t KV_TMEM = tmem_cols_for(KV_DV + HD);
-  // dQ kernel TMEM map
+  // dQ kernel TMEM map (lanes = queries)
+  static constexpr int Q_HALF = Q_KT / 2;
   static constexpr int Q_S = 0;
-  static constexpr int Q_DP = 128;  // dP, then dS (tf32) / dS packed (16-bit)
-  static constexpr int Q_DQ = 256;
+  static constexpr int Q_DP = Q_KT;          // dP; then dS (tf32 in place) or dS packed per half
+  static constexpr int Q_DQ = 2 * Q_KT;
   static constexpr uint32_t Q_TMEM = tmem_cols_for(Q_DQ + HD);
-  static constexpr int NUM_BARS = 24;
-  static constexpr int SMEM_BYTES = 1024 + 2 * TILE_BYTES + 2 * ST * TILE_BYTES + NUM_BARS * 8 + 16;
+  static constexpr int NUM_BARS = 32;
+  static constexpr int KV_SMEM = 1024 + 2 * BIG_TILE + KV_ST * KV_STAGE_BYTES + NUM_BARS * 8 + 16;
+  static constexpr int Q_SMEM = 1024 + 2 * BIG_TILE + Q_ST * Q_STAGE_BYTES + NUM_BARS * 8 + 16;
   static constexpr int THREADS = 320;
-  static_assert(KV_DV + HD <= 512, "TMEM budget (dK/dV kernel)");
+  static_assert(KV_ST >= 1 && Q_ST >= 1, "shared memory budget");
+  static_assert(KV_DV + HD <= 512 && Q_DQ + HD <= 512, "TMEM budget");
   static_assert(HD * EB % 128 == 0, "head dim must fill whole 128-byte rows");
+  static_assert(KV_HALF % 32 == 0 && Q_HALF % 32 == 0, "compute halves are whole 32-column TMEM loads");
+
+  // TMEM column of the A operand for k-step ks of a TS MMA whose A operand was
+  // written by the two compute warpgroups.  tf32: contiguous fp32 columns.
+  // 16-bit: each warpgroup packed its half (half_cols fp32 columns -> half_cols/2
+  // packed columns) at the start of its own half.
+  __device__ static constexpr uint32_t a_col(int ks, int half_cols) {
+    return TF32 ? (uint32_t)(ks * 8)
+                : (uint32_t)((ks / (half_cols / 16)) * half_cols + (ks % (half_cols / 16)) * 8);
+  }
 };
 
+// Load `cols` fp32 TMEM columns starting at taddr into v[].
+template <int N>
+__device__ __forceinline__ void tmem_load_row(uint32_t taddr, float (&v)[N]) {
+#pragma unroll
+  for (int c = 0; c < N / 32; ++c) {
+    uint32_t regs[32];
+    tmem_ld32(taddr + c * 32, regs);
+    tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[c * 32 + i] = __uint_as_float(regs[i]);
+  }
+}
+
+// Store v[] as an MMA A operand: tf32 (one column per value, rounded to
+// nearest) or packed bf16/fp16 pairs (N/2 columns).
+template <typename DT, int N>
+__device__ __forceinline__ void tmem_store_operand(uint32_t taddr, const float (&v)[N]) {
+  if constexpr (sizeof(DT) == 4) {
+#pragma unroll
+    for (int c = 0; c < N / 32; ++c) {
+      uint32_t regs[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) regs[i] = f32_to_tf32_rna(v[c * 32 + i]);
+      tmem_st32(taddr + c * 32, regs);
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < N / 64; ++c) {
+      uint32_t regs[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        regs[i] = std::is_same<DT, __nv_bfloat16>::value ? pack_bf16x2(v[c * 64 + 2 * i], v[c * 64 + 2 * i + 1])
+                                                         : pack_f16x2(v[c * 64 + 2 * i], v[c * 64 + 2 * i + 1]);
+      tmem_st32(taddr + c * 32, regs);
+    }
+    if constexpr (N % 64 == 32) {
+      uint32_t regs[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        regs[i] = std::is_same<DT, __nv_bfloat16>::value ? pack_bf16x2(v[N - 32 + 2 * i], v[N - 32 + 2 * i + 1])
+                                                         : pack_f16x2(v[N - 32 + 2 * i], v[N - 32 + 2 * i + 1]);
+      tmem_st16(taddr + (N / 64) * 32, regs);
+    }
+  }
+}
+
+// Write `cols` (multiple of 32) fp32 TMEM columns of this thread's lane to a
+// row of DT in global memory (zeros when `zero`).
+template <typename DT, int COLS>
+__device__ __forceinline__ void tmem_row_to_global(uint32_t taddr, DT* dst, bool store, bool zero) {
+#pragma unroll
+  for (int c = 0; c < COLS / 32; ++c) {
+    uint32_t regs[32];
+    if (!zero) {
+      tmem_ld32(taddr + c * 32, regs);
+      tmem_wait_ld();
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) regs[i] = 0u;
+    }
+    if (!store) continue;
+    if constexpr (sizeof(DT) == 4) {
+      float4* d4 = reinterpret_cast<float4*>(dst + c * 32);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        d4[i] = make_float4(__uint_as_float(regs[4 * i]), __uint_as_float(regs[4 * i + 1]),
+                            __uint_as_float(regs[4 * i + 2]), __uint_as_float(regs[4 * i + 3]));
+    } else {
+      uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint32_t w[4];
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const float a = __uint_as_float(regs[8 * i + 2 * h]);
+          const float b = __uint_as_float(regs[8 * i + 2 * h + 1]);
+          w[h] = std::is_same<DT, __nv_bfloat16>::value ? pack_bf16x2(a, b) : pack_f16x2(a, b);
+        }
+        d4[i] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
-// dK / dV
+// dK / dV: one CTA per (128-key tile, batch*head)
 // ---------------------------------------------------------------------------
 template <typename DT, int HD>
 __global__ void __launch_bounds__(320, 1)
     attn_bwd_dkdv_sm100(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                        const __grid_constant__ CUtensorMap tm_qm, const __grid_constant__ CUtensorMap tm_dom,
                         const BwdParams p) {
   using C = BwdConfig<DT, HD>;
-  constexpr int ST = C::ST;
+  constexpr int ST = C::KV_ST;
+  constexpr int QT = C::KV_QT;
+  constexpr int HALF = C::KV_HALF;
   constexpr int kKind = DTypeTraits<DT>::kKind;
   constexpr uint32_t kFmt = DTypeTraits<DT>::kFmt;
   constexpr int TMA_WARP = 8, MMA_WARP = 9;
@@ -137,10 +270,13 @@ __global__ void __launch_bounds__(320, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem;
-  uint8_t* sV = sK + C::TILE_BYTES;
-  uint8_t* sQ = sV + C::TILE_BYTES;           // [ST]
-  uint8_t* sdO = sQ + ST * C::TILE_BYTES;     // [ST]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sdO + ST * C::TILE_BYTES);
+  uint8_t* sV = sK + C::BIG_TILE;
+  uint8_t* sStage = sV + C::BIG_TILE;  // per stage: Q, dO [, Q MN copy, dO MN copy]
+  auto sQ = [&](int st) { return sStage + st * C::KV_STAGE_BYTES; };
+  auto sdO = [&](int st) { return sStage + st * C::KV_STAGE_BYTES + C::KV_QTILE; };
+  auto sQm = [&](int st) { return C::TF32 ? sStage + st * C::KV_STAGE_BYTES + 2 * C::KV_QTILE : sQ(st); };
+  auto sdOm = [&](int st) { return C::TF32 ? sStage + st * C::KV_STAGE_BYTES + 3 * C::KV_QTILE : sdO(st); };
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + ST * C::KV_STAGE_BYTES);
   uint64_t* kv_full = bars;
   uint64_t* q_full = kv_full + 1;   // [ST]
   uint64_t* q_empty = q_full + ST;  // [ST]
@@ -157,14 +293,14 @@ __global__ void __launch_bounds__(320, 1)
   const int lane = threadIdx.x & 31;
   const int kt = (int)(blockIdx.x / p.BH);
   const int bh = (int)(blockIdx.x % p.BH);
-  const int key0 = kt * C::BN;
+  const int key0 = kt * C::KV_KEYS;
 
   // Query tiles that see at least one key of this tile.
-  const int n_qt_all = (p.Tq + C::BM - 1) / C::BM;
+  const int n_qt_all = (p.Tq + QT - 1) / QT;
   int qt_first = 0;
   if (p.causal) {
     const int need = key0 - p.causal_offset;  // smallest query index that sees key0
-    qt_first = need <= 0 ? 0 : need / C::BM;
+    qt_first = need <= 0 ? 0 : need / QT;
   }
   const int n_it = max(0, n_qt_all - qt_first);
 
@@ -199,7 +335,7 @@ __global__ void __launch_bounds__(320, 1)
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
       tma_prefetch_desc(&tm_do);
-      mbar_arrive_expect_tx(kv_full, 2 * C::TILE_BYTES);
+      mbar_arrive_expect_tx(kv_full, 2 * C::BIG_TILE);
 #pragma unroll
       for (int b = 0; b < C::KBLK; ++b) {
         tma_load_3d(sK + b * 128 * 128, &tm_k, kv_full, b * C::E128, p.k_row0 + key0, bh);
@@ -209,12 +345,16 @@ __global__ void __launch_bounds__(320, 1)
       for (int it = 0; it < n_it; ++it) {
         const int st = it % ST;
         if (!mbar_wait(&q_empty[st], ((it / ST) & 1) ^ 1, abort_flag, limit, 11)) break;
-        const int row = p.q_row0 + (qt_first + it) * C::BM;
-        mbar_arrive_expect_tx(&q_full[st], 2 * C::TILE_BYTES);
+        const int row = p.q_row0 + (qt_first + it) * QT;
+        mbar_arrive_expect_tx(&q_full[st], C::KV_STAGE_BYTES);
 #pragma unroll
         for (int b = 0; b < C::KBLK; ++b) {
-          tma_load_3d(sQ + st * C::TILE_BYTES + b * 128 * 128, &tm_q, &q_full[st], b * C::E128, row, bh);
-          tma_load_3d(sdO + st * C::TILE_BYTES + b * 128 * 128, &tm_do, &q_full[st], b * C::E128, row, bh);
+          tma_load_3d(sQ(st) + b * QT * 128, &tm_q, &q_full[st], b * C::E128, row, bh);
+          tma_load_3d(sdO(st) + b * QT * 128, &tm_do, &q_full[st], b * C::E128, row, bh);
+          if constexpr (C::TF32) {
+            tma_load_3d(sQm(st) + b * QT * 128, &tm_qm, &q_full[st], b * C::E128, row, bh);
+            tma_load_3d(sdOm(st) + b * QT * 128, &tm_dom, &q_full[st], b * C::E128, row, bh);
+          }
         }
         issued = it + 1;
       }
@@ -230,33 +370,28 @@ __global__ void __launch_bounds__(320, 1)
     __syncwarp();
   } else if (warp == MMA_WARP) {
     if (lane == 0 && n_it > 0) {
-      constexpr uint32_t idesc_s = make_idesc(kFmt, 128, 128, false, false);
+      constexpr uint32_t idesc_s = make_idesc(kFmt, 128, QT, false, false);
       constexpr uint32_t idesc_t = make_idesc(kFmt, 128, HD, false, true);
-      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ), adO = smem_u32(sdO);
-      auto gemm_ss = [&](uint32_t d, uint32_t a_base, uint32_t b_base) {
+      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV);
+      // S^T = K Q^T, dP^T = V dO^T: A is the 128-key tile, B the streamed query tile.
+      auto gemm_ss = [&](uint32_t d, uint32_t a_tile, uint32_t b_tile) {
 #pragma unroll
-        for (int ks = 0; ks < C::KSTEP_S; ++ks) {
-          const uint32_t off = (ks >> 2) * (128 * 128) + (ks & 3) * 32;
-          umma_ss<kKind>(d, make_sdesc_sw128(a_base + off, 16, 1024), make_sdesc_sw128(b_base + off, 16, 1024),
-                         idesc_s, ks > 0 ? 1u : 0u);
-        }
+        for (int ks = 0; ks < C::KSTEP_S; ++ks)
+          umma_ss<kKind>(d, kmajor_desc(a_tile, 128, ks), kmajor_desc(b_tile, QT, ks), idesc_s, ks > 0 ? 1u : 0u);
       };
-      // A operand columns: tf32 operands are contiguous; 16-bit operands are
-      // packed by each compute warpgroup into its own 64-column half.
-      auto gemm_ts = [&](uint32_t d, uint32_t a_tmem, uint32_t b_base, bool acc) {
+      // dV += P^T dO, dK += dS^T Q: A from TMEM, B = MN-major query tile.
+      auto gemm_ts = [&](uint32_t d, uint32_t a_base, uint32_t b_tile, bool acc) {
 #pragma unroll
-        for (int ks = 0; ks < C::KSTEP_T; ++ks) {
-          const uint32_t a_col = C::TF32 ? ks * 8 : (ks >> 2) * 64 + (ks & 3) * 8;
-          umma_ts<kKind>(d, a_tmem + a_col, make_sdesc_sw128(b_base + ks * C::K_PER * 128, 128 * 128, 1024),
-                         idesc_t, (acc || ks > 0) ? 1u : 0u);
-        }
+        for (int ks = 0; ks < QT / C::K_PER; ++ks)
+          umma_ts<kKind>(d, a_base + C::a_col(ks, HALF), mnmajor_desc<C::TF32>(b_tile, QT, ks, C::K_PER), idesc_t,
+                         (acc || ks > 0) ? 1u : 0u);
       };
       bool ok = mbar_wait(kv_full, 0, abort_flag, limit, 12) && mbar_wait(&q_full[0], 0, abort_flag, limit, 13);
       if (ok) {
         tc_fence_after();
-        gemm_ss(tbase + C::KV_S, aK, aQ);
+        gemm_ss(tbase + C::KV_S, aK, smem_u32(sQ(0)));
         umma_commit(s_full);
-        gemm_ss(tbase + C::KV_DP, aV, adO);
+        gemm_ss(tbase + C::KV_DP, aV, smem_u32(sdO(0)));
         umma_commit(dp_full);
       }
       for (int it = 0; ok && it < n_it; ++it) {
@@ -266,16 +401,16 @@ __global__ void __launch_bounds__(320, 1)
           if (!(ok = mbar_wait(s_free, it & 1, abort_flag, limit, 14))) break;
           if (!(ok = mbar_wait(&q_full[st1], ((it + 1) / ST) & 1, abort_flag, limit, 15))) break;
           tc_fence_after();
-          gemm_ss(tbase + C::KV_S, aK, aQ + st1 * C::TILE_BYTES);
+          gemm_ss(tbase + C::KV_S, aK, smem_u32(sQ(st1)));
           umma_commit(s_full);
         }
         if (!(ok = mbar_wait(p_full, it & 1, abort_flag, limit, 16))) break;
         tc_fence_after();
-        gemm_ts(tbase + C::KV_DV, tbase + C::KV_P, adO + st * C::TILE_BYTES, it > 0);
-        gemm_ts(tbase + C::KV_DK, tbase + C::KV_DP, aQ + st * C::TILE_BYTES, it > 0);
+        gemm_ts(tbase + C::KV_DV, tbase + C::KV_P, smem_u32(sdOm(st)), it > 0);
+        gemm_ts(tbase + C::KV_DK, tbase + C::KV_DP, smem_u32(sQm(st)), it > 0);
         umma_commit(&q_empty[st]);
         if (it + 1 < n_it) {
-          gemm_ss(tbase + C::KV_DP, aV, adO + st1 * C::TILE_BYTES);
+          gemm_ss(tbase + C::KV_DP, aV, smem_u32(sdO(st1)));
           umma_commit(dp_full);
         } else {
           umma_commit(acc_full);
@@ -289,37 +424,27 @@ __global__ void __launch_bounds__(320, 1)
     __syncwarp();
   } else {
     // --------------------------- compute warps ---------------------------
-    const int h = threadIdx.x >> 7;  // column half
-    const int r = threadIdx.x & 127; // key row inside the tile (TMEM lane)
+    const int h = threadIdx.x >> 7;   // column half
+    const int r = threadIdx.x & 127;  // key row inside the tile (TMEM lane)
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const int key = key0 + r;
+    const bool key_ok = key < p.Tk;
     const float sl2 = p.scale_log2;
     const float scale = p.scale;
     const float* lse_bh = p.lse + (size_t)bh * p.q_rows_alloc + p.q_row0;
     const float* delta_bh = p.delta + (size_t)bh * p.Tq;
     bool ok = true;
     for (int it = 0; it < n_it; ++it) {
-      const int q0 = (qt_first + it) * C::BM + h * 64;
+      const int q0 = (qt_first + it) * QT + h * HALF;
       if (!(ok = mbar_wait(s_full, it & 1, abort_flag, limit, 17))) break;
       tc_fence_after();
-      float s[64];
-      {
-        uint32_t regs[32];
-        tmem_ld32(tbase + lane_off + C::KV_S + h * 64, regs);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[i] = __uint_as_float(regs[i]);
-        tmem_ld32(tbase + lane_off + C::KV_S + h * 64 + 32, regs);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[32 + i] = __uint_as_float(regs[i]);
-      }
+      float s[HALF];
+      tmem_load_row(tbase + lane_off + C::KV_S + h * HALF, s);
       tc_fence_before();
       mbar_arrive(s_free);
-      // P^T = exp2(S^T * scale*log2e - lse*log2e), masked.
-      const bool key_ok = key < p.Tk;
+      // P^T = exp2(S^T * scale*log2e - lse*log2e), masked
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
+      for (int c = 0; c < HALF; ++c) {
         const int q = q0 + c;
         const bool vis = key_ok && q < p.Tq && (!p.causal || key <= q + p.causal_offset);
         const float L = vis ? __ldg(lse_bh + q) * 1.4426950408889634f : 0.f;
@@ -327,45 +452,20 @@ __global__ void __launch_bounds__(320, 1)
       }
       if (!(ok = mbar_wait(dp_full, it & 1, abort_flag, limit, 18))) break;
       tc_fence_after();
-      float dsv[64];
-      {
-        uint32_t regs[32];
-        tmem_ld32(tbase + lane_off + C::KV_DP + h * 64, regs);
-        tmem_wait_ld();
+      float dsv[HALF];
+      tmem_load_row(tbase + lane_off + C::KV_DP + h * HALF, dsv);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) dsv[i] = __uint_as_float(regs[i]);
-        tmem_ld32(tbase + lane_off + C::KV_DP + h * 64 + 32, regs);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) dsv[32 + i] = __uint_as_float(regs[i]);
-      }
-#pragma unroll
-      for (int c = 0; c < 64; ++c) {
+      for (int c = 0; c < HALF; ++c) {
         const int q = q0 + c;
         const float dl = q < p.Tq ? __ldg(delta_bh + q) : 0.f;
         dsv[c] = s[c] * (dsv[c] - dl) * scale;
       }
       if constexpr (C::TF32) {
-        uint32_t regs[32];
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) regs[i] = f32_to_tf32_rna(s[half * 32 + i]);
-          tmem_st32(tbase + lane_off + C::KV_P + h * 64 + half * 32, regs);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) regs[i] = f32_to_tf32_rna(dsv[half * 32 + i]);
-          tmem_st32(tbase + lane_off + C::KV_DP + h * 64 + half * 32, regs);
-        }
+        tmem_store_operand<DT>(tbase + lane_off + C::KV_P + h * HALF, s);
+        tmem_store_operand<DT>(tbase + lane_off + C::KV_DP + h * HALF, dsv);
       } else {
-        uint32_t regs[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          regs[i] = (kFmt == 1) ? pack_bf16x2(s[2 * i], s[2 * i + 1]) : pack_f16x2(s[2 * i], s[2 * i + 1]);
-        tmem_st32(tbase + lane_off + C::KV_DP + h * 64 + 32, regs);
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          regs[i] = (kFmt == 1) ? pack_bf16x2(dsv[2 * i], dsv[2 * i + 1]) : pack_f16x2(dsv[2 * i], dsv[2 * i + 1]);
-        tmem_st32(tbase + lane_off + C::KV_DP + h * 64, regs);
+        tmem_store_operand<DT>(tbase + lane_off + C::KV_DP + h * HALF + HALF / 2, s);
+        tmem_store_operand<DT>(tbase + lane_off + C::KV_DP + h * HALF, dsv);
       }
       tmem_wait_st();
       tc_fence_before();
@@ -375,48 +475,12 @@ __global__ void __launch_bounds__(320, 1)
     if (ok && n_it > 0) ok = mbar_wait(acc_full, 0, abort_flag, limit, 19);
     if (ok) {
       tc_fence_after();
-      const bool row_ok = key < p.Tk;
       const size_t row_index = (size_t)bh * p.k_rows_alloc + p.k_row0 + key;
-      DT* dk_row = reinterpret_cast<DT*>(p.dk) + row_index * HD;
-      DT* dv_row = reinterpret_cast<DT*>(p.dv) + row_index * HD;
-#pragma unroll
-      for (int c = 0; c < HD / 64; ++c) {
-        const int col = h * (HD / 2) + c * 32;
-#pragma unroll
-        for (int which = 0; which < 2; ++which) {
-          uint32_t regs[32];
-          if (n_it > 0) {
-            tmem_ld32(tbase + lane_off + (which ? C::KV_DV : C::KV_DK) + col, regs);
-            tmem_wait_ld();
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) regs[i] = 0u;
-          }
-          if (row_ok) {
-            DT* dst = (which ? dv_row : dk_row) + col;
-            if constexpr (C::EB == 4) {
-              float4* d4 = reinterpret_cast<float4*>(dst);
-#pragma unroll
-              for (int i = 0; i < 8; ++i)
-                d4[i] = make_float4(__uint_as_float(regs[4 * i]), __uint_as_float(regs[4 * i + 1]),
-                                    __uint_as_float(regs[4 * i + 2]), __uint_as_float(regs[4 * i + 3]));
-            } else {
-              uint4* d4 = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                uint32_t w[4];
-#pragma unroll
-                for (int hh = 0; hh < 4; ++hh) {
-                  const float a = __uint_as_float(regs[8 * i + 2 * hh]);
-                  const float b = __uint_as_float(regs[8 * i + 2 * hh + 1]);
-                  w[hh] = (kFmt == 1) ? pack_bf16x2(a, b) : pack_f16x2(a, b);
-                }
-                d4[i] = make_uint4(w[0], w[1], w[2], w[3]);
-              }
-            }
-          }
-        }
-      }
+      const int col = h * (HD / 2);
+      tmem_row_to_global<DT, HD / 2>(tbase + lane_off + C::KV_DK + col,
+                                     reinterpret_cast<DT*>(p.dk) + row_index * HD + col, key_ok, n_it == 0);
+      tmem_row_to_global<DT, HD / 2>(tbase + lane_off + C::KV_DV + col,
+                                     reinterpret_cast<DT*>(p.dv) + row_index * HD + col, key_ok, n_it == 0);
     }
   }
 
@@ -429,15 +493,17 @@ __global__ void __launch_bounds__(320, 1)
 }
 
 // ---------------------------------------------------------------------------
-// dQ
+// dQ: one CTA per (128-query tile, batch*head)
 // ---------------------------------------------------------------------------
 template <typename DT, int HD>
 __global__ void __launch_bounds__(320, 1)
     attn_bwd_dq_sm100(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                      const BwdParams p, int n_qtiles) {
+                      const __grid_constant__ CUtensorMap tm_km, const BwdParams p, int n_qtiles) {
   using C = BwdConfig<DT, HD>;
-  constexpr int ST = C::ST;
+  constexpr int ST = C::Q_ST;
+  constexpr int KT = C::Q_KT;
+  constexpr int HALF = C::Q_HALF;
   constexpr int kKind = DTypeTraits<DT>::kKind;
   constexpr uint32_t kFmt = DTypeTraits<DT>::kFmt;
   constexpr int TMA_WARP = 8, MMA_WARP = 9;
@@ -445,10 +511,12 @@ __global__ void __launch_bounds__(320, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
-  uint8_t* sdO = sQ + C::TILE_BYTES;
-  uint8_t* sK = sdO + C::TILE_BYTES;   // [ST]
-  uint8_t* sV = sK + ST * C::TILE_BYTES;  // [ST]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + ST * C::TILE_BYTES);
+  uint8_t* sdO = sQ + C::BIG_TILE;
+  uint8_t* sStage = sdO + C::BIG_TILE;  // per stage: K, V [, K MN copy]
+  auto sK = [&](int st) { return sStage + st * C::Q_STAGE_BYTES; };
+  auto sV = [&](int st) { return sStage + st * C::Q_STAGE_BYTES + C::Q_KTILE; };
+  auto sKm = [&](int st) { return C::TF32 ? sStage + st * C::Q_STAGE_BYTES + 2 * C::Q_KTILE : sK(st); };
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + ST * C::Q_STAGE_BYTES);
   uint64_t* q_full = bars;
   uint64_t* k_full = q_full + 1;    // [ST]
   uint64_t* k_empty = k_full + ST;  // [ST]
@@ -473,11 +541,11 @@ __global__ void __launch_bounds__(320, 1)
     qt = (int)(blockIdx.x % n_qtiles);
     bh = (int)(blockIdx.x / n_qtiles);
   }
-  const int n_kv_all = (p.Tk + C::BN - 1) / C::BN;
+  const int n_kv_all = (p.Tk + KT - 1) / KT;
   int n_kv = n_kv_all;
   if (p.causal) {
-    const int last_row = min(qt * C::BM + C::BM - 1, p.Tq - 1) + p.causal_offset;
-    n_kv = last_row < 0 ? 0 : min(n_kv_all, last_row / C::BN + 1);
+    const int last_row = min(qt * C::Q_ROWS + C::Q_ROWS - 1, p.Tq - 1) + p.causal_offset;
+    n_kv = last_row < 0 ? 0 : min(n_kv_all, last_row / KT + 1);
   }
 
   if (threadIdx.x == 0) {
@@ -513,8 +581,8 @@ __global__ void __launch_bounds__(320, 1)
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
       tma_prefetch_desc(&tm_do);
-      const int qrow = p.q_row0 + qt * C::BM;
-      mbar_arrive_expect_tx(q_full, 2 * C::TILE_BYTES);
+      const int qrow = p.q_row0 + qt * C::Q_ROWS;
+      mbar_arrive_expect_tx(q_full, 2 * C::BIG_TILE);
 #pragma unroll
       for (int b = 0; b < C::KBLK; ++b) {
         tma_load_3d(sQ + b * 128 * 128, &tm_q, q_full, b * C::E128, qrow, bh);
@@ -524,18 +592,20 @@ __global__ void __launch_bounds__(320, 1)
       for (int j = 0; j < n_kv; ++j) {
         const int st = j % ST;
         const uint32_t ph = (j / ST) & 1;
-        const int row = p.k_row0 + j * C::BN;
+        const int row = p.k_row0 + j * KT;
         if (!mbar_wait(&k_empty[st], ph ^ 1, abort_flag, limit, 21)) break;
-        mbar_arrive_expect_tx(&k_full[st], C::TILE_BYTES);
+        mbar_arrive_expect_tx(&k_full[st], (C::TF32 ? 2 : 1) * C::Q_KTILE);
 #pragma unroll
-        for (int b = 0; b < C::KBLK; ++b)
-          tma_load_3d(sK + st * C::TILE_BYTES + b * 128 * 128, &tm_k, &k_full[st], b * C::E128, row, bh);
+        for (int b = 0; b < C::KBLK; ++b) {
+          tma_load_3d(sK(st) + b * KT * 128, &tm_k, &k_full[st], b * C::E128, row, bh);
+          if constexpr (C::TF32) tma_load_3d(sKm(st) + b * KT * 128, &tm_km, &k_full[st], b * C::E128, row, bh);
+        }
         issued_k = j + 1;
         if (!mbar_wait(&v_empty[st], ph ^ 1, abort_flag, limit, 22)) break;
-        mbar_arrive_expect_tx(&v_full[st], C::TILE_BYTES);
+        mbar_arrive_expect_tx(&v_full[st], C::Q_KTILE);
 #pragma unroll
         for (int b = 0; b < C::KBLK; ++b)
-          tma_load_3d(sV + st * C::TILE_BYTES + b * 128 * 128, &tm_v, &v_full[st], b * C::E128, row, bh);
+          tma_load_3d(sV(st) + b * KT * 128, &tm_v, &v_full[st], b * C::E128, row, bh);
         issued_v = j + 1;
       }
       if (*abort_flag) {
@@ -553,24 +623,22 @@ __global__ void __launch_bounds__(320, 1)
     __syncwarp();
   } else if (warp == MMA_WARP) {
     if (lane == 0 && n_kv > 0) {
-      constexpr uint32_t idesc_s = make_idesc(kFmt, 128, 128, false, false);
+      constexpr uint32_t idesc_s = make_idesc(kFmt, 128, KT, false, false);
       constexpr uint32_t idesc_t = make_idesc(kFmt, 128, HD, false, true);
-      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ), adO = smem_u32(sdO);
-      auto gemm_ss = [&](uint32_t d, uint32_t a_base, uint32_t b_base) {
+      const uint32_t aQ = smem_u32(sQ), adO = smem_u32(sdO);
+      // S = Q K^T, dP = dO V^T: A is the 128-query tile, B the streamed key tile.
+      auto gemm_ss = [&](uint32_t d, uint32_t a_tile, uint32_t b_tile) {
 #pragma unroll
-        for (int ks = 0; ks < C::KSTEP_S; ++ks) {
-          const uint32_t off = (ks >> 2) * (128 * 128) + (ks & 3) * 32;
-          umma_ss<kKind>(d, make_sdesc_sw128(a_base + off, 16, 1024), make_sdesc_sw128(b_base + off, 16, 1024),
-                         idesc_s, ks > 0 ? 1u : 0u);
-        }
+        for (int ks = 0; ks < C::KSTEP_S; ++ks)
+          umma_ss<kKind>(d, kmajor_desc(a_tile, 128, ks), kmajor_desc(b_tile, KT, ks), idesc_s, ks > 0 ? 1u : 0u);
       };
       bool ok = mbar_wait(q_full, 0, abort_flag, limit, 23) && mbar_wait(&k_full[0], 0, abort_flag, limit, 24) &&
                 mbar_wait(&v_full[0], 0, abort_flag, limit, 25);
       if (ok) {
         tc_fence_after();
-        gemm_ss(tbase + C::Q_S, aQ, aK);
+        gemm_ss(tbase + C::Q_S, aQ, smem_u32(sK(0)));
         umma_commit(s_full);
-        gemm_ss(tbase + C::Q_DP, adO, aV);
+        gemm_ss(tbase + C::Q_DP, adO, smem_u32(sV(0)));
         umma_commit(dp_full);
         umma_commit(&v_empty[0]);
       }
@@ -582,23 +650,21 @@ __global__ void __launch_bounds__(320, 1)
           if (!(ok = mbar_wait(s_free, j & 1, abort_flag, limit, 26))) break;
           if (!(ok = mbar_wait(&k_full[st1], ph1, abort_flag, limit, 27))) break;
           tc_fence_after();
-          gemm_ss(tbase + C::Q_S, aQ, aK + st1 * C::TILE_BYTES);
+          gemm_ss(tbase + C::Q_S, aQ, smem_u32(sK(st1)));
           umma_commit(s_full);
         }
         if (!(ok = mbar_wait(ds_full, j & 1, abort_flag, limit, 28))) break;
         tc_fence_after();
+        const uint32_t bK = smem_u32(sKm(st));
 #pragma unroll
-        for (int ks = 0; ks < C::KSTEP_T; ++ks) {
-          const uint32_t a_col = C::TF32 ? ks * 8 : (ks >> 2) * 64 + (ks & 3) * 8;
-          umma_ts<kKind>(tbase + C::Q_DQ, tbase + C::Q_DP + a_col,
-                         make_sdesc_sw128(aK + st * C::TILE_BYTES + ks * C::K_PER * 128, 128 * 128, 1024), idesc_t,
-                         (j > 0 || ks > 0) ? 1u : 0u);
-        }
+        for (int ks = 0; ks < KT / C::K_PER; ++ks)
+          umma_ts<kKind>(tbase + C::Q_DQ, tbase + C::Q_DP + C::a_col(ks, HALF),
+                         mnmajor_desc<C::TF32>(bK, KT, ks, C::K_PER), idesc_t, (j > 0 || ks > 0) ? 1u : 0u);
         umma_commit(&k_empty[st]);
         if (j + 1 < n_kv) {
           if (!(ok = mbar_wait(&v_full[st1], ph1, abort_flag, limit, 29))) break;
           tc_fence_after();
-          gemm_ss(tbase + C::Q_DP, adO, aV + st1 * C::TILE_BYTES);
+          gemm_ss(tbase + C::Q_DP, adO, smem_u32(sV(st1)));
           umma_commit(dp_full);
           umma_commit(&v_empty[st1]);
         } else {
@@ -616,7 +682,7 @@ __global__ void __launch_bounds__(320, 1)
     const int h = threadIdx.x >> 7;   // key-column half
     const int r = threadIdx.x & 127;  // query row (TMEM lane)
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    const int q = qt * C::BM + r;
+    const int q = qt * C::Q_ROWS + r;
     const bool q_ok = q < p.Tq;
     const float sl2 = p.scale_log2;
     const float scale = p.scale;
@@ -628,57 +694,23 @@ __global__ void __launch_bounds__(320, 1)
     if (!q_ok) vis = -1;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      const int kc0 = j * C::BN + h * 64;  // first key of this thread's half
+      const int kc0 = j * KT + h * HALF;  // first key of this thread's half
       if (!(ok = mbar_wait(s_full, j & 1, abort_flag, limit, 30))) break;
       tc_fence_after();
-      float s[64];
-      {
-        uint32_t regs[32];
-        tmem_ld32(tbase + lane_off + C::Q_S + h * 64, regs);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[i] = __uint_as_float(regs[i]);
-        tmem_ld32(tbase + lane_off + C::Q_S + h * 64 + 32, regs);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[32 + i] = __uint_as_float(regs[i]);
-      }
+      float s[HALF];
+      tmem_load_row(tbase + lane_off + C::Q_S + h * HALF, s);
       tc_fence_before();
       mbar_arrive(s_free);
       const int lim = vis - kc0;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) s[c] = (c <= lim) ? ex2_approx(fmaf(s[c], sl2, -L)) : 0.f;
+      for (int c = 0; c < HALF; ++c) s[c] = (c <= lim) ? ex2_approx(fmaf(s[c], sl2, -L)) : 0.f;
       if (!(ok = mbar_wait(dp_full, j & 1, abort_flag, limit, 31))) break;
       tc_fence_after();
-      float dsv[64];
-      {
-        uint32_t regs[32];
-        tmem_ld32(tbase + lane_off + C::Q_DP + h * 64, regs);
-        tmem_wait_ld();
+      float dsv[HALF];
+      tmem_load_row(tbase + lane_off + C::Q_DP + h * HALF, dsv);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) dsv[i] = __uint_as_float(regs[i]);
-        tmem_ld32(tbase + lane_off + C::Q_DP + h * 64 + 32, regs);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) dsv[32 + i] = __uint_as_float(regs[i]);
-      }
-#pragma unroll
-      for (int c = 0; c < 64; ++c) dsv[c] = s[c] * (dsv[c] - dl) * scale;
-      if constexpr (C::TF32) {
-        uint32_t regs[32];
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) regs[i] = f32_to_tf32_rna(dsv[half * 32 + i]);
-          tmem_st32(tbase + lane_off + C::Q_DP + h * 64 + half * 32, regs);
-        }
-      } else {
-        uint32_t regs[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          regs[i] = (kFmt == 1) ? pack_bf16x2(dsv[2 * i], dsv[2 * i + 1]) : pack_f16x2(dsv[2 * i], dsv[2 * i + 1]);
-        tmem_st32(tbase + lane_off + C::Q_DP + h * 64, regs);
-      }
+      for (int c = 0; c < HALF; ++c) dsv[c] = s[c] * (dsv[c] - dl) * scale;
+      tmem_store_operand<DT>(tbase + lane_off + C::Q_DP + h * HALF, dsv);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(ds_full);
@@ -686,41 +718,9 @@ __global__ void __launch_bounds__(320, 1)
     if (ok && n_kv > 0) ok = mbar_wait(acc_full, 0, abort_flag, limit, 32);
     if (ok) {
       tc_fence_after();
-      DT* dq_row = reinterpret_cast<DT*>(p.dq) + lrow * HD;
-#pragma unroll
-      for (int c = 0; c < HD / 64; ++c) {
-        const int col = h * (HD / 2) + c * 32;
-        uint32_t regs[32];
-        if (n_kv > 0) {
-          tmem_ld32(tbase + lane_off + C::Q_DQ + col, regs);
-          tmem_wait_ld();
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) regs[i] = 0u;
-        }
-        if (q_ok) {
-          if constexpr (C::EB == 4) {
-            float4* d4 = reinterpret_cast<float4*>(dq_row + col);
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              d4[i] = make_float4(__uint_as_float(regs[4 * i]), __uint_as_float(regs[4 * i + 1]),
-                                  __uint_as_float(regs[4 * i + 2]), __uint_as_float(regs[4 * i + 3]));
-          } else {
-            uint4* d4 = reinterpret_cast<uint4*>(dq_row + col);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              uint32_t w[4];
-#pragma unroll
-              for (int hh = 0; hh < 4; ++hh) {
-                const float a = __uint_as_float(regs[8 * i + 2 * hh]);
-                const float b = __uint_as_float(regs[8 * i + 2 * hh + 1]);
-                w[hh] = (kFmt == 1) ? pack_bf16x2(a, b) : pack_f16x2(a, b);
-              }
-              d4[i] = make_uint4(w[0], w[1], w[2], w[3]);
-            }
-          }
-        }
-      }
+      const int col = h * (HD / 2);
+      tmem_row_to_global<DT, HD / 2>(tbase + lane_off + C::Q_DQ + col,
+                                     reinterpret_cast<DT*>(p.dq) + lrow * HD + col, q_ok, n_kv == 0);
     }
   }
 

@@ -13,6 +13,9 @@
 //   warp  4*NQ      : TMA producer (Q once, then K/V tiles through ST stages).
 //   warp  4*NQ+1    : tcgen05.mma issuer (one elected lane).
 //
+//   V is the MN-major B operand of P V: 128B swizzle for 16-bit types, the
+//   32-byte-granule variant for tf32.
+//
 //   TMEM columns:  S_k = Q_k K^T  at [k*BN, (k+1)*BN)            (fp32)
 //                  P_k written over S_k by the softmax warps       (tf32, or bf16/fp16 packed in pairs)
 //                  O_k += P_k V   at [NQ*BN + k*HD, ... + HD)      (fp32)
@@ -215,10 +218,8 @@ __global__ void __launch_bounds__(NQ * 128 + 64, 1)
         const uint32_t d = tbase + k * BN;
 #pragma unroll
         for (int ks = 0; ks < C::KSTEP_S; ++ks) {
-          const uint64_t a = make_sdesc_sw128(sQ_addr + k * C::Q_TILE_BYTES + (ks >> 2) * (BM * 128) + (ks & 3) * 32,
-                                              16, 1024);
-          const uint64_t b = make_sdesc_sw128(
-              sK_addr + st * C::KV_TILE_BYTES + (ks >> 2) * (BN * 128) + (ks & 3) * 32, 16, 1024);
+          const uint64_t a = kmajor_desc(sQ_addr + k * C::Q_TILE_BYTES, BM, ks);
+          const uint64_t b = kmajor_desc(sK_addr + st * C::KV_TILE_BYTES, BN, ks);
           umma_ss<kKind>(d, a, b, idesc_s, ks > 0 ? 1u : 0u);
         }
       };
@@ -227,8 +228,7 @@ __global__ void __launch_bounds__(NQ * 128 + 64, 1)
 #pragma unroll
         for (int ks = 0; ks < C::KSTEP_PV; ++ks) {
           const uint32_t a = tbase + k * BN + ks * 8;
-          const uint64_t b =
-              make_sdesc_sw128(sV_addr + st * C::KV_TILE_BYTES + ks * C::K_PER_PV * 128, BN * 128, 1024);
+          const uint64_t b = mnmajor_desc<C::EB == 4>(sV_addr + st * C::KV_TILE_BYTES, BN, ks, C::K_PER_PV);
           umma_ts<kKind>(d, a, b, idesc_pv, (acc || ks > 0) ? 1u : 0u);
         }
       };

@@ -123,10 +123,13 @@ __global__ void attn_fwd_simt(const DT* __restrict__ q, const DT* __restrict__ k
     lse[(size_t)bh * p.q_rows_alloc + p.q_row0 + i] = l > A(0) ? (float)(m + acc_log(l)) : -INFINITY;
 }
 
-// delta_i = sum_d O_i[d] * dO_i[d]
+// delta_i = sum_d O_i[d] * dO_i[d].  For double I/O the row logsumexp is
+// also recomputed in double (lse_acc), because the float lse of the C ABI
+// would cap the backward at float accuracy.
 template <typename DT>
-__global__ void attn_bwd_delta_simt(const DT* __restrict__ o, const DT* __restrict__ dO, AccT<DT>* __restrict__ delta,
-                                    SimtParams p) {
+__global__ void attn_bwd_delta_simt(const DT* __restrict__ q, const DT* __restrict__ k, const DT* __restrict__ o,
+                                    const DT* __restrict__ dO, AccT<DT>* __restrict__ delta,
+                                    AccT<DT>* __restrict__ lse_acc, SimtParams p) {
   using A = AccT<DT>;
   const long long w = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -137,13 +140,44 @@ __global__ void attn_bwd_delta_simt(const DT* __restrict__ o, const DT* __restri
   for (int d = lane; d < p.D; d += 32) s += to_acc(o[row + d]) * to_acc(dO[row + d]);
   s = warp_sum(s);
   if (lane == 0) delta[(size_t)bh * p.Tq + i] = s;
+  if (lse_acc != nullptr) {
+    const size_t kbase = ((size_t)bh * p.k_rows_alloc + p.k_row0) * p.D;
+    A qv[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      const int d = lane + 32 * t;
+      qv[t] = d < p.D ? to_acc(q[row + d]) : A(0);
+    }
+    A m = -INFINITY, l = 0;
+    const int last = simt_last_key(p, i);
+    for (int j = 0; j <= last; ++j) {
+      A x = 0;
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        const int d = lane + 32 * t;
+        if (d < p.D) x += qv[t] * to_acc(k[kbase + (size_t)j * p.D + d]);
+      }
+      x = warp_sum(x) * (A)p.scale;
+      const A mn = x > m ? x : m;
+      l = l * acc_exp(m - mn) + acc_exp(x - mn);
+      m = mn;
+    }
+    if (lane == 0) lse_acc[(size_t)bh * p.Tq + i] = m + acc_log(l);
+  }
+}
+
+// Row logsumexp for the backward: the recomputed one when present, else the forward's.
+template <typename A>
+__device__ __forceinline__ A row_lse(const float* lse, const A* lse_acc, const SimtParams& p, int bh, int i) {
+  return lse_acc != nullptr ? lse_acc[(size_t)bh * p.Tq + i] : (A)lse[(size_t)bh * p.q_rows_alloc + p.q_row0 + i];
 }
 
 // dQ_i = scale * sum_j P_ij (dP_ij - delta_i) K_j, with P_ij = exp(scale*q_i.k_j - lse_i), dP_ij = dO_i.v_j
 template <typename DT>
 __global__ void attn_bwd_dq_simt(const DT* __restrict__ q, const DT* __restrict__ k, const DT* __restrict__ v,
                                  const DT* __restrict__ dO, const float* __restrict__ lse,
-                                 const AccT<DT>* __restrict__ delta, DT* __restrict__ dq, SimtParams p) {
+                                 const AccT<DT>* __restrict__ lse_acc, const AccT<DT>* __restrict__ delta,
+                                 DT* __restrict__ dq, SimtParams p) {
   using A = AccT<DT>;
   const long long w = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -160,7 +194,7 @@ __global__ void attn_bwd_dq_simt(const DT* __restrict__ q, const DT* __restrict_
     acc[t] = A(0);
   }
   const A scale = (A)p.scale;
-  const A L = (A)lse[(size_t)bh * p.q_rows_alloc + p.q_row0 + i];
+  const A L = row_lse(lse, lse_acc, p, bh, i);
   const A dl = delta[(size_t)bh * p.Tq + i];
   const int last = simt_last_key(p, i);
   for (int j = 0; j <= last; ++j) {
@@ -195,8 +229,8 @@ __global__ void attn_bwd_dq_simt(const DT* __restrict__ q, const DT* __restrict_
 template <typename DT>
 __global__ void attn_bwd_dkdv_simt(const DT* __restrict__ q, const DT* __restrict__ k, const DT* __restrict__ v,
                                    const DT* __restrict__ dO, const float* __restrict__ lse,
-                                   const AccT<DT>* __restrict__ delta, DT* __restrict__ dk, DT* __restrict__ dv,
-                                   SimtParams p) {
+                                   const AccT<DT>* __restrict__ lse_acc, const AccT<DT>* __restrict__ delta,
+                                   DT* __restrict__ dk, DT* __restrict__ dv, SimtParams p) {
   using A = AccT<DT>;
   const long long w = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -229,7 +263,7 @@ __global__ void attn_bwd_dkdv_simt(const DT* __restrict__ q, const DT* __restric
     }
     s = warp_sum(s);
     dp = warp_sum(dp);
-    const A L = (A)lse[(size_t)bh * p.q_rows_alloc + p.q_row0 + i];
+    const A L = row_lse(lse, lse_acc, p, bh, i);
     const A pij = acc_exp(s * scale - L);
     const A ds = pij * (dp - delta[(size_t)bh * p.Tq + i]) * scale;
 #pragma unroll

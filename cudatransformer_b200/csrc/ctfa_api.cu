@@ -65,8 +65,11 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // 3-D map over an allocation [BH][rows][D] with a (128-byte x box_rows x 1)
-// box and 128-byte swizzle.  Rows past `rows` read as zero.
-int make_map(CUtensorMap* map, const void* base, int dtype, int D, int rows, int BH, int box_rows) {
+// box and 128-byte swizzle.  Rows past `rows` read as zero.  mn32: 128-byte
+// swizzle with 32-byte granules, the layout of tf32 operands that the MMA
+// reads N-major (V in the forward, the MN-major copies in the backward).
+int make_map(CUtensorMap* map, const void* base, int dtype, int D, int rows, int BH, int box_rows,
+             bool mn32 = false) {
   auto fn = encode_fn();
   if (!fn) return fail(CTFA_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
   const size_t eb = dtype_bytes(dtype);
@@ -78,7 +81,8 @@ int make_map(CUtensorMap* map, const void* base, int dtype, int D, int rows, int
   cuuint32_t box[3] = {(cuuint32_t)(128 / eb), (cuuint32_t)box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  mn32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(CTFA_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
   return CTFA_OK;
 }
@@ -118,7 +122,7 @@ int launch_fwd_tc(const Problem& pr, const void* q, const void* k, const void* v
   int s;
   if ((s = make_map(&mq, q, pr.dtype, HD, pr.q_rows, pr.B * pr.H, 128)) != CTFA_OK) return s;
   if ((s = make_map(&mk, k, pr.dtype, HD, pr.k_rows, pr.B * pr.H, BN)) != CTFA_OK) return s;
-  if ((s = make_map(&mv, v, pr.dtype, HD, pr.k_rows, pr.B * pr.H, BN)) != CTFA_OK) return s;
+  if ((s = make_map(&mv, v, pr.dtype, HD, pr.k_rows, pr.B * pr.H, BN, sizeof(DT) == 4)) != CTFA_OK) return s;
   FwdParams p;
   p.BH = pr.B * pr.H;
   p.Tq = pr.Tq;
@@ -163,6 +167,54 @@ SimtParams simt_params(const Problem& pr) {
 
 unsigned warps_grid(long long warps) { return (unsigned)((warps * 32 + 255) / 256); }
 
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Round-to-nearest tf32 copies of up to four fp32 tensors (one launch).  The
+// tensor core truncates fp32 operands to tf32 (drops 13 mantissa bits toward
+// zero); feeding it rounded values removes that bias.
+struct RoundJob {
+  const float4* in[4];
+  float4* out[4];
+  long long n4;  // float4 per tensor
+  int count;
+};
+
+__global__ void __launch_bounds__(256) round_tf32_kernel(RoundJob job) {
+  const int t = blockIdx.y;
+  const float4* in = job.in[t];
+  float4* out = job.out[t];
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < job.n4;
+       i += (long long)gridDim.x * blockDim.x) {
+    float4 x = in[i];
+    x.x = __uint_as_float(f32_to_tf32_rna(x.x));
+    x.y = __uint_as_float(f32_to_tf32_rna(x.y));
+    x.z = __uint_as_float(f32_to_tf32_rna(x.z));
+    x.w = __uint_as_float(f32_to_tf32_rna(x.w));
+    out[i] = x;
+  }
+}
+
+int launch_round(const void* const* in, void* const* out, int count, size_t elems, cudaStream_t stream) {
+  RoundJob job;
+  for (int i = 0; i < 4; ++i) {
+    job.in[i] = i < count ? reinterpret_cast<const float4*>(in[i]) : nullptr;
+    job.out[i] = i < count ? reinterpret_cast<float4*>(out[i]) : nullptr;
+  }
+  job.n4 = (long long)(elems / 4);
+  job.count = count;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long want = (job.n4 + 255) / 256;
+  dim3 grid((unsigned)std::min<long long>(want, (long long)sms * 8), count);
+  round_tf32_kernel<<<grid, 256, 0, stream>>>(job);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? CTFA_OK : cuda_fail(e, "launch round_tf32_kernel");
+}
+
+// fp32 I/O on the tensor cores works on rounded operand copies in the workspace.
+bool needs_rounding(int dtype, int D) { return dtype == CTFA_DTYPE_F32 && (D == 64 || D == 128); }
+
 template <typename DT>
 int launch_fwd_simt(const Problem& pr, const void* q, const void* k, const void* v, void* o, float* lse,
                     cudaStream_t stream) {
@@ -173,19 +225,31 @@ int launch_fwd_simt(const Problem& pr, const void* q, const void* k, const void*
   return e == cudaSuccess ? CTFA_OK : cuda_fail(e, "launch attn_fwd_simt");
 }
 
+size_t fwd_workspace(const Problem& pr) {
+  if (!needs_rounding(pr.dtype, pr.D)) return 0;
+  return 3 * align256((size_t)pr.B * pr.H * pr.q_rows * pr.D * sizeof(float));
+}
+
 int forward_impl(const Problem& pr, const void* q, const void* k, const void* v, void* o, float* lse,
-                 cudaStream_t stream) {
+                 void* ws, cudaStream_t stream) {
+  int s;
   if (tensor_core_shape(pr)) {
     bool sm100 = false;
-    int s = device_is_sm100(&sm100);
+    s = device_is_sm100(&sm100);
     if (s != CTFA_OK) return s;
     if (!sm100) return fail(CTFA_ERR_UNSUPPORTED, "tensor-core attention kernels need an sm_100 (B200) device");
     if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
       return fail(CTFA_ERR_MISALIGNED, "q/k/v/o must be 16-byte aligned");
     switch (pr.dtype) {
-      case CTFA_DTYPE_F32:
-        return pr.D == 64 ? launch_fwd_tc<float, 64, 2, 128, 2>(pr, q, k, v, o, lse, stream)
-                          : launch_fwd_tc<float, 128, 1, 64, 2>(pr, q, k, v, o, lse, stream);
+      case CTFA_DTYPE_F32: {
+        const size_t n = (size_t)pr.B * pr.H * pr.q_rows * pr.D;
+        char* w = reinterpret_cast<char*>(ws);
+        void* r[3] = {w, w + align256(n * 4), w + 2 * align256(n * 4)};
+        const void* in[3] = {q, k, v};
+        if ((s = launch_round(in, r, 3, n, stream)) != CTFA_OK) return s;
+        return pr.D == 64 ? launch_fwd_tc<float, 64, 2, 128, 2>(pr, r[0], r[1], r[2], o, lse, stream)
+                          : launch_fwd_tc<float, 128, 1, 64, 2>(pr, r[0], r[1], r[2], o, lse, stream);
+      }
       case CTFA_DTYPE_BF16:
         return pr.D == 64 ? launch_fwd_tc<__nv_bfloat16, 64, 2, 128, 3>(pr, q, k, v, o, lse, stream)
                           : launch_fwd_tc<__nv_bfloat16, 128, 2, 128, 2>(pr, q, k, v, o, lse, stream);
@@ -227,33 +291,53 @@ Problem full_problem(int B, int H, int T, int D, int dtype, int causal) {
 // ---------------------------------------------------------------------------
 // Backward
 // ---------------------------------------------------------------------------
-size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
-
 size_t bwd_workspace(const Problem& pr) {
   const size_t rows = (size_t)pr.B * pr.H * pr.Tq;
-  if (tensor_core_shape(pr)) return align256(rows * sizeof(float));  // delta
-  return align256(rows * (pr.dtype == CTFA_DTYPE_F64 ? sizeof(double) : sizeof(float)));
+  if (tensor_core_shape(pr)) {
+    size_t ws = align256(rows * sizeof(float));  // delta
+    if (needs_rounding(pr.dtype, pr.D) && pr.D == 64)  // rounded q, k, v, dO (fp32 D=128 runs SIMT)
+      ws += 4 * align256(rows * pr.D * sizeof(float));
+    return ws;
+  }
+  if (pr.dtype == CTFA_DTYPE_F64) return 2 * align256(rows * sizeof(double));  // delta + lse in double
+  return align256(rows * sizeof(float));
+}
+
+// Optional profiling events: ev[0] before the first launch, ev[1] after the
+// delta pass, ev[2] after the dK/dV pass, ev[3] after the dQ pass.
+void record(cudaEvent_t* ev, int i, cudaStream_t stream) {
+  if (ev) cudaEventRecord(ev[i], stream);
 }
 
 template <typename DT>
 int launch_bwd_simt(const Problem& pr, const void* q, const void* k, const void* v, const void* o, const void* dO,
-                    const float* lse, void* dq, void* dk, void* dv, void* ws, cudaStream_t stream) {
+                    const float* lse, void* dq, void* dk, void* dv, void* ws, cudaStream_t stream,
+                    cudaEvent_t* ev) {
   using A = AccT<DT>;
   SimtParams p = simt_params(pr);
   A* delta = reinterpret_cast<A*>(ws);
-  attn_bwd_delta_simt<DT><<<warps_grid((long long)p.BH * p.Tq), 256, 0, stream>>>((const DT*)o, (const DT*)dO,
-                                                                                   delta, p);
-  attn_bwd_dq_simt<DT><<<warps_grid((long long)p.BH * p.Tq), 256, 0, stream>>>(
-      (const DT*)q, (const DT*)k, (const DT*)v, (const DT*)dO, lse, delta, (DT*)dq, p);
+  // double I/O: the row logsumexp is recomputed in double (second workspace array)
+  A* lse_acc = std::is_same<DT, double>::value
+                   ? reinterpret_cast<A*>(reinterpret_cast<char*>(ws) + align256((size_t)p.BH * p.Tq * sizeof(A)))
+                   : nullptr;
+  record(ev, 0, stream);
+  attn_bwd_delta_simt<DT><<<warps_grid((long long)p.BH * p.Tq), 256, 0, stream>>>(
+      (const DT*)q, (const DT*)k, (const DT*)o, (const DT*)dO, delta, lse_acc, p);
+  record(ev, 1, stream);
   attn_bwd_dkdv_simt<DT><<<warps_grid((long long)p.BH * p.Tk), 256, 0, stream>>>(
-      (const DT*)q, (const DT*)k, (const DT*)v, (const DT*)dO, lse, delta, (DT*)dk, (DT*)dv, p);
+      (const DT*)q, (const DT*)k, (const DT*)v, (const DT*)dO, lse, lse_acc, delta, (DT*)dk, (DT*)dv, p);
+  record(ev, 2, stream);
+  attn_bwd_dq_simt<DT><<<warps_grid((long long)p.BH * p.Tq), 256, 0, stream>>>(
+      (const DT*)q, (const DT*)k, (const DT*)v, (const DT*)dO, lse, lse_acc, delta, (DT*)dq, p);
+  record(ev, 3, stream);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? CTFA_OK : cuda_fail(e, "launch attn_bwd_simt");
 }
 
 template <typename DT, int HD>
 int launch_bwd_tc(const Problem& pr, const void* q, const void* k, const void* v, const void* o, const void* dO,
-                  const float* lse, void* dq, void* dk, void* dv, void* ws, cudaStream_t stream) {
+                  const void* dO_mma, const float* lse, void* dq, void* dk, void* dv, void* ws, cudaStream_t stream,
+                  cudaEvent_t* ev) {
   using C = BwdConfig<DT, HD>;
   const int BH = pr.B * pr.H;
   float* delta = reinterpret_cast<float*>(ws);
@@ -266,16 +350,34 @@ int launch_bwd_tc(const Problem& pr, const void* q, const void* k, const void* v
   pp.o = o;
   pp.dO = dO;
   pp.delta = delta;
+  pp.dO_round = (dO_mma != dO) ? reinterpret_cast<float*>(const_cast<void*>(dO_mma)) : nullptr;
+  if (!std::is_same<DT, float>::value) record(ev, 0, stream);
   attn_bwd_prep<DT, HD><<<warps_grid(pp.rows), 256, 0, stream>>>(pp);
+  record(ev, 1, stream);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch attn_bwd_prep");
-  // 2. dK/dV (key-stationary) and dQ (query-stationary)
-  CUtensorMap mq, mk, mv, mdo;
+  // 2. dK/dV (key-stationary) and dQ (query-stationary).  Each kernel has its
+  // own box heights; tf32 operands read N-major get a 32-byte-granule map.
+  constexpr bool kMN32 = C::TF32;
+  CUtensorMap kv_q, kv_do, kv_k, kv_v, kv_qm, kv_dom, q_q, q_do, q_k, q_v, q_km;
   int s;
-  if ((s = make_map(&mq, q, pr.dtype, HD, pr.q_rows, BH, C::BM)) != CTFA_OK) return s;
-  if ((s = make_map(&mdo, dO, pr.dtype, HD, pr.q_rows, BH, C::BM)) != CTFA_OK) return s;
-  if ((s = make_map(&mk, k, pr.dtype, HD, pr.k_rows, BH, C::BN)) != CTFA_OK) return s;
-  if ((s = make_map(&mv, v, pr.dtype, HD, pr.k_rows, BH, C::BN)) != CTFA_OK) return s;
+  if ((s = make_map(&kv_q, q, pr.dtype, HD, pr.q_rows, BH, C::KV_QT)) != CTFA_OK) return s;
+  if ((s = make_map(&kv_do, dO_mma, pr.dtype, HD, pr.q_rows, BH, C::KV_QT)) != CTFA_OK) return s;
+  if ((s = make_map(&kv_k, k, pr.dtype, HD, pr.k_rows, BH, C::KV_KEYS)) != CTFA_OK) return s;
+  if ((s = make_map(&kv_v, v, pr.dtype, HD, pr.k_rows, BH, C::KV_KEYS)) != CTFA_OK) return s;
+  if ((s = make_map(&q_q, q, pr.dtype, HD, pr.q_rows, BH, C::Q_ROWS)) != CTFA_OK) return s;
+  if ((s = make_map(&q_do, dO_mma, pr.dtype, HD, pr.q_rows, BH, C::Q_ROWS)) != CTFA_OK) return s;
+  if ((s = make_map(&q_k, k, pr.dtype, HD, pr.k_rows, BH, C::Q_KT)) != CTFA_OK) return s;
+  if ((s = make_map(&q_v, v, pr.dtype, HD, pr.k_rows, BH, C::Q_KT)) != CTFA_OK) return s;
+  if (kMN32) {
+    if ((s = make_map(&kv_qm, q, pr.dtype, HD, pr.q_rows, BH, C::KV_QT, true)) != CTFA_OK) return s;
+    if ((s = make_map(&kv_dom, dO_mma, pr.dtype, HD, pr.q_rows, BH, C::KV_QT, true)) != CTFA_OK) return s;
+    if ((s = make_map(&q_km, k, pr.dtype, HD, pr.k_rows, BH, C::Q_KT, true)) != CTFA_OK) return s;
+  } else {
+    kv_qm = kv_q;
+    kv_dom = kv_do;
+    q_km = q_k;
+  }
   BwdParams p;
   p.BH = BH;
   p.Tq = pr.Tq;
@@ -294,28 +396,33 @@ int launch_bwd_tc(const Problem& pr, const void* q, const void* k, const void* v
   p.dk = dk;
   p.dv = dv;
   p.wait_limit_ns = g_wait_limit_ns;
-  const int n_kt = (pr.Tk + C::BN - 1) / C::BN;
-  const int n_qt = (pr.Tq + C::BM - 1) / C::BM;
+  const int n_kt = (pr.Tk + C::KV_KEYS - 1) / C::KV_KEYS;
+  const int n_qt = (pr.Tq + C::Q_ROWS - 1) / C::Q_ROWS;
   auto kdkdv = attn_bwd_dkdv_sm100<DT, HD>;
-  e = cudaFuncSetAttribute(kdkdv, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+  e = cudaFuncSetAttribute(kdkdv, cudaFuncAttributeMaxDynamicSharedMemorySize, C::KV_SMEM);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attn_bwd_dkdv_sm100)");
-  kdkdv<<<(unsigned)((long long)n_kt * BH), C::THREADS, C::SMEM_BYTES, stream>>>(mq, mk, mv, mdo, p);
+  kdkdv<<<(unsigned)((long long)n_kt * BH), C::THREADS, C::KV_SMEM, stream>>>(kv_q, kv_k, kv_v, kv_do, kv_qm,
+                                                                              kv_dom, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch attn_bwd_dkdv_sm100");
+  record(ev, 2, stream);
   auto kdq = attn_bwd_dq_sm100<DT, HD>;
-  e = cudaFuncSetAttribute(kdq, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+  e = cudaFuncSetAttribute(kdq, cudaFuncAttributeMaxDynamicSharedMemorySize, C::Q_SMEM);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attn_bwd_dq_sm100)");
-  kdq<<<(unsigned)((long long)n_qt * BH), C::THREADS, C::SMEM_BYTES, stream>>>(mq, mk, mv, mdo, p, n_qt);
+  kdq<<<(unsigned)((long long)n_qt * BH), C::THREADS, C::Q_SMEM, stream>>>(q_q, q_k, q_v, q_do, q_km, p, n_qt);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch attn_bwd_dq_sm100");
+  record(ev, 3, stream);
   return CTFA_OK;
 }
 
 int backward_impl(const Problem& pr, const void* q, const void* k, const void* v, const void* o, const void* dO,
-                  const float* lse, void* dq, void* dk, void* dv, void* ws, cudaStream_t stream) {
+                  const float* lse, void* dq, void* dk, void* dv, void* ws, cudaStream_t stream,
+                  cudaEvent_t* ev = nullptr) {
+  int s;
   if (tensor_core_shape(pr)) {
     bool sm100 = false;
-    int s = device_is_sm100(&sm100);
+    s = device_is_sm100(&sm100);
     if (s != CTFA_OK) return s;
     if (!sm100) return fail(CTFA_ERR_UNSUPPORTED, "tensor-core attention kernels need an sm_100 (B200) device");
     if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(dO) || !aligned16(dq) ||
@@ -323,21 +430,31 @@ int backward_impl(const Problem& pr, const void* q, const void* k, const void* v
       return fail(CTFA_ERR_MISALIGNED, "q/k/v/o/dO/dq/dk/dv must be 16-byte aligned");
     switch (pr.dtype) {
       case CTFA_DTYPE_F32:
-        if (pr.D == 64) return launch_bwd_tc<float, 64>(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, stream);
+        if (pr.D == 64) {
+          const size_t rows = (size_t)pr.B * pr.H * pr.Tq;
+          const size_t n = rows * pr.D;
+          char* w = reinterpret_cast<char*>(ws) + align256(rows * sizeof(float));
+          void* r[4] = {w, w + align256(n * 4), w + 2 * align256(n * 4), w + 3 * align256(n * 4)};
+          const void* in[3] = {q, k, v};
+          record(ev, 0, stream);
+          if ((s = launch_round(in, r, 3, n, stream)) != CTFA_OK) return s;
+          // the delta pass writes the rounded dO (r[3]) the GEMMs read
+          return launch_bwd_tc<float, 64>(pr, r[0], r[1], r[2], o, dO, r[3], lse, dq, dk, dv, ws, stream, ev);
+        }
         break;  // fp32 D=128 does not fit the tensor-core backward's shared memory: SIMT below
       case CTFA_DTYPE_BF16:
-        return pr.D == 64 ? launch_bwd_tc<__nv_bfloat16, 64>(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, stream)
-                          : launch_bwd_tc<__nv_bfloat16, 128>(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, stream);
+        return pr.D == 64 ? launch_bwd_tc<__nv_bfloat16, 64>(pr, q, k, v, o, dO, dO, lse, dq, dk, dv, ws, stream, ev)
+                          : launch_bwd_tc<__nv_bfloat16, 128>(pr, q, k, v, o, dO, dO, lse, dq, dk, dv, ws, stream, ev);
       default:
-        return pr.D == 64 ? launch_bwd_tc<__half, 64>(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, stream)
-                          : launch_bwd_tc<__half, 128>(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, stream);
+        return pr.D == 64 ? launch_bwd_tc<__half, 64>(pr, q, k, v, o, dO, dO, lse, dq, dk, dv, ws, stream, ev)
+                          : launch_bwd_tc<__half, 128>(pr, q, k, v, o, dO, dO, lse, dq, dk, dv, ws, stream, ev);
     }
   }
   switch (pr.dtype) {
-    case CTFA_DTYPE_F32: return launch_bwd_simt<float>(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, stream);
-    case CTFA_DTYPE_BF16: return launch_bwd_simt<__nv_bfloat16>(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, stream);
-    case CTFA_DTYPE_F16: return launch_bwd_simt<__half>(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, stream);
-    default: return launch_bwd_simt<double>(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, stream);
+    case CTFA_DTYPE_F32: return launch_bwd_simt<float>(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, stream, ev);
+    case CTFA_DTYPE_BF16: return launch_bwd_simt<__nv_bfloat16>(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, stream, ev);
+    case CTFA_DTYPE_F16: return launch_bwd_simt<__half>(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, stream, ev);
+    default: return launch_bwd_simt<double>(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, stream, ev);
   }
 }
 
@@ -382,12 +499,25 @@ extern "C" int ctfa_set_wait_limit_ns(unsigned long long ns) {
   return CTFA_OK;
 }
 
+extern "C" size_t ctfa_forward_workspace_bytes(int B, int H, int T, int D, int dtype) {
+  if (check_common(B, H, T, D, dtype) != CTFA_OK) return 0;
+  return fwd_workspace(full_problem(B, H, T, D, dtype, 0));
+}
+
 extern "C" int ctfa_forward(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H, int T,
-                            int D, int dtype, int causal, void* stream) {
+                            int D, int dtype, int causal, void* workspace, size_t workspace_bytes, void* stream) {
   int s = check_common(B, H, T, D, dtype);
   if (s != CTFA_OK) return s;
   if (!q || !k || !v || !o) return fail(CTFA_ERR_INVALID_ARGUMENT, "q, k, v and o must be non-null");
-  return forward_impl(full_problem(B, H, T, D, dtype, causal), q, k, v, o, lse, (cudaStream_t)stream);
+  Problem pr = full_problem(B, H, T, D, dtype, causal);
+  const size_t need = fwd_workspace(pr);
+  if (need > 0) {
+    if (!workspace || workspace_bytes < need)
+      return fail(CTFA_ERR_WORKSPACE, "workspace needs " + std::to_string(need) + " bytes");
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+      return fail(CTFA_ERR_MISALIGNED, "workspace must be 256-byte aligned");
+  }
+  return forward_impl(pr, q, k, v, o, lse, workspace, (cudaStream_t)stream);
 }
 
 extern "C" size_t ctfa_backward_workspace_bytes(int B, int H, int T, int D, int dtype) {
@@ -410,6 +540,24 @@ extern "C" int ctfa_backward(const void* q, const void* k, const void* v, const 
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
     return fail(CTFA_ERR_MISALIGNED, "workspace must be 256-byte aligned");
   return backward_impl(pr, q, k, v, o, dO, lse, dq, dk, dv, workspace, (cudaStream_t)stream);
+}
+
+extern "C" int ctfa_backward_with_events(const void* q, const void* k, const void* v, const void* o, const void* dO,
+                                         const float* lse, void* dq, void* dk, void* dv, void* workspace,
+                                         size_t workspace_bytes, int B, int H, int T, int D, int dtype, int causal,
+                                         void* stream, void** events) {
+  int s = check_common(B, H, T, D, dtype);
+  if (s != CTFA_OK) return s;
+  if (!q || !k || !v || !o || !dO || !lse || !dq || !dk || !dv || !events)
+    return fail(CTFA_ERR_INVALID_ARGUMENT, "tensors and events must be non-null");
+  Problem pr = full_problem(B, H, T, D, dtype, causal);
+  const size_t need = bwd_workspace(pr);
+  if (!workspace || workspace_bytes < need)
+    return fail(CTFA_ERR_WORKSPACE, "workspace needs " + std::to_string(need) + " bytes");
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return fail(CTFA_ERR_MISALIGNED, "workspace must be 256-byte aligned");
+  return backward_impl(pr, q, k, v, o, dO, lse, dq, dk, dv, workspace, (cudaStream_t)stream,
+                       reinterpret_cast<cudaEvent_t*>(events));
 }
 
 extern "C" int ctfa_check_device_error(void* stream) {

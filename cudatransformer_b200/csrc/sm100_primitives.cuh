@@ -195,16 +195,45 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 // Descriptors
 // ---------------------------------------------------------------------------
 // Shared-memory matrix descriptor (tcgen05 format): start address, leading
-// byte offset, stride byte offset (all >> 4), version 1 at bit 46, swizzle
-// mode at bits 61..63 (2 = 128-byte swizzle).
-__device__ __forceinline__ uint64_t make_sdesc_sw128(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+// byte offset, stride byte offset (all >> 4), version 1 at bit 46, layout
+// (swizzle) type at bits 61..63.
+//   kLayoutSW128      (2): 128-byte swizzle, 16-byte granules XOR row%8.  K-major
+//                          operands of every type; MN-major 16-bit operands.
+//   kLayoutSW128Base32 (1): 128-byte swizzle, 32-byte granules XOR row%4.  The
+//                          only MN-major layout the tensor core reads correctly
+//                          for tf32 (measured: the 16-byte-granule layout gives
+//                          zeros).  K rows are 128 bytes apart, SBO = 4 rows.
+constexpr uint32_t kLayoutSW128 = 2;
+constexpr uint32_t kLayoutSW128Base32 = 1;
+
+__device__ __forceinline__ uint64_t make_sdesc(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                               uint32_t layout) {
   uint64_t d = 0;
   d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
   d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
   d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= (uint64_t)1u << 46;
-  d |= (uint64_t)2u << 61;
+  d |= (uint64_t)layout << 61;
   return d;
+}
+
+__device__ __forceinline__ uint64_t make_sdesc_sw128(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  return make_sdesc(smem_addr, lbo_bytes, sbo_bytes, kLayoutSW128);
+}
+
+// K-major operand tile stored as 128-byte column blocks of `rows` rows each
+// (TMA box = 128 bytes x rows, 128B swizzle).  k-step `ks` covers 32 bytes of
+// the reduction dim: 16 bf16/fp16 or 8 tf32 elements.
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile_addr, int rows, int ks) {
+  return make_sdesc(tile_addr + (ks >> 2) * (rows * 128) + (ks & 3) * 32, 16, 1024, kLayoutSW128);
+}
+
+// MN-major operand tile [red_rows][N] stored as 128-byte column blocks of
+// `red_rows` rows each.  k-step `ks` covers k_per rows of the reduction dim.
+template <bool kTF32>
+__device__ __forceinline__ uint64_t mnmajor_desc(uint32_t tile_addr, int red_rows, int ks, int k_per) {
+  return make_sdesc(tile_addr + ks * k_per * 128, red_rows * 128, kTF32 ? 512 : 1024,
+                    kTF32 ? kLayoutSW128Base32 : kLayoutSW128);
 }
 
 // Instruction descriptor for kind::f16 / kind::tf32 with fp32 accumulation.

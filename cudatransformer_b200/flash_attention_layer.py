@@ -84,6 +84,18 @@ class FlashAttentionLayer:
             raise RuntimeError(f"unsupported dtype {q.dtype}")
         return B, T, _DTYPES[q.dtype]
 
+    def _forward(self, lib, q, k, v, out, lse, B, T, dt):
+        ws_bytes = lib.ctfa_forward_workspace_bytes(B, self.numHeads, T, self.headDim, dt)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
+        with torch.cuda.device(q.device):
+            status = lib.ctfa_forward(
+                _ptr(q), _ptr(k), _ptr(v), _ptr(out), _ptr(lse), B, self.numHeads, T, self.headDim, dt,
+                int(self.causal), _ptr(ws), ws_bytes, _stream_handle(q.device),
+            )
+            _lib.check(status, "ctfa_forward")
+            if _lib.sync_check_enabled():
+                _lib.check(lib.ctfa_check_device_error(_stream_handle(q.device)), "ctfa_forward (device)")
+
     # -- API -------------------------------------------------------------
     def computeAttention(
         self, queries: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, saveStates: bool = False
@@ -92,14 +104,7 @@ class FlashAttentionLayer:
         lib = _lib.load()
         output = torch.empty_like(queries)
         lse = torch.empty((B, self.numHeads, T), dtype=torch.float32, device=queries.device)
-        with torch.cuda.device(queries.device):
-            status = lib.ctfa_forward(
-                _ptr(queries), _ptr(keys), _ptr(values), _ptr(output), _ptr(lse),
-                B, self.numHeads, T, self.headDim, dt, int(self.causal), _stream_handle(queries.device),
-            )
-            _lib.check(status, "ctfa_forward")
-            if _lib.sync_check_enabled():
-                _lib.check(lib.ctfa_check_device_error(_stream_handle(queries.device)), "ctfa_forward (device)")
+        self._forward(lib, queries, keys, values, output, lse, B, T, dt)
         if saveStates:
             self.cachedLSE = lse
             self.cachedMaxScores = lse.to(queries.dtype)
@@ -120,14 +125,7 @@ class FlashAttentionLayer:
             # (FlashAttentionLayer.cu:114-127).
             output = torch.empty_like(queries)
             lse = torch.empty((B, self.numHeads, T), dtype=torch.float32, device=queries.device)
-            with torch.cuda.device(queries.device):
-                _lib.check(
-                    lib.ctfa_forward(
-                        _ptr(queries), _ptr(keys), _ptr(values), _ptr(output), _ptr(lse),
-                        B, self.numHeads, T, self.headDim, dt, int(self.causal), _stream_handle(queries.device),
-                    ),
-                    "ctfa_forward (recompute)",
-                )
+            self._forward(lib, queries, keys, values, output, lse, B, T, dt)
         dq = torch.empty_like(queries)
         dk = torch.empty_like(keys)
         dv = torch.empty_like(values)

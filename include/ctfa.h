@@ -58,11 +58,19 @@ const char* ctfa_last_error_message(void);
  * at flash_attention.cu:57-169).  causal = 0 reproduces the reference's
  * semantics (every query attends every key); causal = 1 masks key j > query i.
  * lse may be NULL when the caller does not keep it for the backward pass.
+ * workspace: ctfa_forward_workspace_bytes(...) bytes of device memory,
+ * 256-byte aligned (NULL when that is 0).
  * D: any value in [1, 256]; D = 64 and D = 128 with f32/bf16/f16 run on the
  * tcgen05 tensor-core kernels, everything else on SIMT kernels.
  */
 int ctfa_forward(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H, int T, int D,
-                 int dtype, int causal, void* stream);
+                 int dtype, int causal, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Bytes of device workspace ctfa_forward needs (0 except for fp32 I/O on the
+ * tensor cores, where it holds the round-to-nearest tf32 copies of q, k, v:
+ * the MMA itself truncates fp32 operands to tf32, which costs a factor ~4 in
+ * accuracy).  workspace may be NULL when this is 0. */
+size_t ctfa_forward_workspace_bytes(int B, int H, int T, int D, int dtype);
 
 /* Bytes of device workspace ctfa_backward needs for this problem. */
 size_t ctfa_backward_workspace_bytes(int B, int H, int T, int D, int dtype);
@@ -80,6 +88,17 @@ size_t ctfa_backward_workspace_bytes(int B, int H, int T, int D, int dtype);
 int ctfa_backward(const void* q, const void* k, const void* v, const void* o, const void* dO, const float* lse,
                   void* dq, void* dk, void* dv, void* workspace, size_t workspace_bytes, int B, int H, int T,
                   int D, int dtype, int causal, void* stream);
+
+/*
+ * Profiling variant of ctfa_backward (no reference counterpart): identical
+ * work, and it records events[0..3] (cudaEvent_t) on `stream` before the
+ * first launch and after the delta, dK/dV and dQ passes, so a caller can time
+ * each kernel on its own launch stream.
+ */
+int ctfa_backward_with_events(const void* q, const void* k, const void* v, const void* o, const void* dO,
+                              const float* lse, void* dq, void* dk, void* dv, void* workspace,
+                              size_t workspace_bytes, int B, int H, int T, int D, int dtype, int causal,
+                              void* stream, void** events);
 
 /*
  * Bound, in nanoseconds, on every wait inside the kernels (default 2e9).  A

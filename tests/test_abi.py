@@ -41,16 +41,26 @@ FAKE = ctypes.c_void_p(4096)  # never dereferenced: every call below fails valid
 @pytest.mark.parametrize(
     "args,status",
     [
-        ((None, FAKE, FAKE, FAKE, None, 1, 1, 8, 64, 0, 0, None), _lib.CTFA_ERR_INVALID_ARGUMENT),
-        ((FAKE, FAKE, FAKE, FAKE, None, 0, 1, 8, 64, 0, 0, None), _lib.CTFA_ERR_INVALID_ARGUMENT),
-        ((FAKE, FAKE, FAKE, FAKE, None, 1, 1, -3, 64, 0, 0, None), _lib.CTFA_ERR_INVALID_ARGUMENT),
-        ((FAKE, FAKE, FAKE, FAKE, None, 1, 1, 8, 64, 7, 0, None), _lib.CTFA_ERR_INVALID_ARGUMENT),
-        ((FAKE, FAKE, FAKE, FAKE, None, 1, 1, 8, 300, 0, 0, None), _lib.CTFA_ERR_UNSUPPORTED),
+        ((None, FAKE, FAKE, FAKE, None, 1, 1, 8, 64, 0, 0, None, 0, None), _lib.CTFA_ERR_INVALID_ARGUMENT),
+        ((FAKE, FAKE, FAKE, FAKE, None, 0, 1, 8, 64, 0, 0, None, 0, None), _lib.CTFA_ERR_INVALID_ARGUMENT),
+        ((FAKE, FAKE, FAKE, FAKE, None, 1, 1, -3, 64, 0, 0, None, 0, None), _lib.CTFA_ERR_INVALID_ARGUMENT),
+        ((FAKE, FAKE, FAKE, FAKE, None, 1, 1, 8, 64, 7, 0, None, 0, None), _lib.CTFA_ERR_INVALID_ARGUMENT),
+        ((FAKE, FAKE, FAKE, FAKE, None, 1, 1, 8, 300, 0, 0, None, 0, None), _lib.CTFA_ERR_UNSUPPORTED),
+        # fp32 on the tensor-core path needs the rounding workspace
+        ((FAKE, FAKE, FAKE, FAKE, None, 1, 1, 8, 64, 0, 0, None, 0, None), _lib.CTFA_ERR_WORKSPACE),
     ],
 )
 def test_forward_argument_validation(ctfa, args, status):
     assert ctfa.ctfa_forward(*args) == status
     assert _lib.last_error()
+
+
+def test_workspace_sizes(ctfa):
+    n = 2 * 3 * 100 * 64
+    assert ctfa.ctfa_forward_workspace_bytes(2, 3, 100, 64, _lib.CTFA_DTYPE_F32) >= 3 * n * 4
+    assert ctfa.ctfa_forward_workspace_bytes(2, 3, 100, 64, _lib.CTFA_DTYPE_BF16) == 0
+    assert ctfa.ctfa_forward_workspace_bytes(2, 3, 100, 32, _lib.CTFA_DTYPE_F32) == 0  # SIMT path
+    assert ctfa.ctfa_backward_workspace_bytes(2, 3, 100, 64, _lib.CTFA_DTYPE_F32) >= 4 * n * 4
 
 
 def test_backward_argument_validation(ctfa):

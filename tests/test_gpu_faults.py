@@ -52,4 +52,4 @@ def test_misaligned_tensor_core_input_is_rejected(cuda_device, ctfa):
     o = torch.empty(B * H * T * D, device=cuda_device, dtype=torch.bfloat16)
     st = torch.cuda.current_stream().cuda_stream
     assert ctfa.ctfa_forward(x.data_ptr(), x.data_ptr(), x.data_ptr(), o.data_ptr(), None, B, H, T, D,
-                             _lib.CTFA_DTYPE_BF16, 0, st) == _lib.CTFA_ERR_MISALIGNED
+                             _lib.CTFA_DTYPE_BF16, 0, None, 0, st) == _lib.CTFA_ERR_MISALIGNED

@@ -52,7 +52,7 @@ def test_simt_paths(cuda_device, kind, D, causal):
     if kind == "f32" and D == 128:
         tol = TOL["f32"]  # the fp32 D=128 forward is tensor-core (tf32)
     for name, e in errors(ours, ref).items():
-        assert e < tol, (name, e)
+        assert e < (max(tol, 1e-6) if name == "lse" else tol), (name, e)  # lse is fp32 in every mode
 
 
 @pytest.mark.parametrize("causal", [False, True])
@@ -119,7 +119,7 @@ def test_outputs_do_not_write_past_their_rows(cuda_device, ctfa):
     lse = torch.empty(B * H * T, device=cuda_device, dtype=torch.float32)
     st = torch.cuda.current_stream().cuda_stream
     _lib.check(ctfa.ctfa_forward(q.data_ptr(), k.data_ptr(), v.data_ptr(), views["o"].data_ptr(), lse.data_ptr(),
-                                 B, H, T, D, _lib.CTFA_DTYPE_BF16, 1, st), "fwd")
+                                 B, H, T, D, _lib.CTFA_DTYPE_BF16, 1, None, 0, st), "fwd")
     ws = torch.empty(ctfa.ctfa_backward_workspace_bytes(B, H, T, D, _lib.CTFA_DTYPE_BF16), dtype=torch.uint8,
                      device=cuda_device)
     _lib.check(ctfa.ctfa_backward(q.data_ptr(), k.data_ptr(), v.data_ptr(), views["o"].data_ptr(), do.data_ptr(),
