@@ -1,0 +1,163 @@
+// Drop-in replacement for CudaTransformer's cuda_transformer/FlashAttentionLayer.cu.
+//
+// Same template, same public members and signatures as the reference
+// (FlashAttentionLayer.cu:13-150), same Tensor<DType> layout ([B, H, T, D],
+// contiguous row-major) and the same include guard, so AttentionLayer.cu,
+// TransformerBlockLayer.cu, NanoGPT.cu and the pybind module compile against
+// it unchanged.  The two kernel launches of the reference
+// (flashAttention<<<>>> at FlashAttentionLayer.cu:76-79/123-126 and
+// flashAttentionBackward<<<>>> at :133-140) become calls into the C ABI of
+// libctfa_b200.so (include/ctfa.h): tcgen05 tensor-core kernels for float,
+// __nv_bfloat16 and __half with head dim 64/128, SIMT kernels otherwise
+// (double, other head dims up to 256).
+//
+// Build: put this directory before the reference's cuda_transformer/ on the
+// include path and include this header before the reference's headers (or
+// replace the reference file with it), add include/ to the path and link
+// libctfa_b200.so.  Allocation follows the reference: outputs and caches are
+// Tensor / cudaMakeShared buffers on the legacy default stream.
+//
+// Additions (all defaulted, existing call sites unchanged):
+//   * bool causal (constructor's optional third argument, default false = the
+//     reference's behaviour): masks key j > query i.
+//   * cachedLSE: fp32 logsumexp per row, what the kernels keep for the
+//     backward.  cachedMaxScores holds the same logsumexp in DType and
+//     cachedDenominators holds ones, so exp(s - max) / denom is still the
+//     softmax for code that reads the old fields.
+// Errors: every non-zero status from the library throws std::runtime_error
+// (the reference throws from cudaMakeShared and ignores launch errors).
+#include "ModuleLayer.cu"
+#include "ctfa.h"
+
+#ifndef FLASH_ATTENTION_LAYER
+#define FLASH_ATTENTION_LAYER
+
+namespace ctfa_dropin {
+
+template <typename T>
+struct DtypeCode;
+template <>
+struct DtypeCode<float> {
+  static constexpr int value = CTFA_DTYPE_F32;
+};
+template <>
+struct DtypeCode<__nv_bfloat16> {
+  static constexpr int value = CTFA_DTYPE_BF16;
+};
+template <>
+struct DtypeCode<__half> {
+  static constexpr int value = CTFA_DTYPE_F16;
+};
+template <>
+struct DtypeCode<double> {
+  static constexpr int value = CTFA_DTYPE_F64;
+};
+
+inline void check(int status, const char* where) {
+  if (status != CTFA_OK)
+    throw std::runtime_error(std::string(where) + ": " + ctfa_status_string(status) + ": " +
+                             ctfa_last_error_message());
+}
+
+}  // namespace ctfa_dropin
+
+template <typename DType = float>
+struct FlashAttentionLayer {
+  int headDim = 1;   /// Dimension of each attention head.
+  int numHeads = 1;  /// Number of attention heads.
+
+  // Cached values from the forward pass for the backward pass.
+  std::shared_ptr<DType[]> cachedMaxScores = nullptr;
+  std::shared_ptr<DType[]> cachedDenominators = nullptr;
+  std::shared_ptr<DType[]> cachedOutput = nullptr;
+  int cachedBatchSize = 0;
+  int cachedSequenceLength = 0;
+
+  bool causal = false;                        /// key j visible to query i iff j <= i
+  std::shared_ptr<float[]> cachedLSE = nullptr;  /// fp32 logsumexp per row
+
+  FlashAttentionLayer(int headDim, int numHeads, bool causal = false)
+      : headDim(headDim), numHeads(numHeads), causal(causal) {}
+
+  std::shared_ptr<FlashAttentionLayer<DType>> clone() const {
+    return std::make_shared<FlashAttentionLayer<DType>>(headDim, numHeads, causal);
+  }
+
+  /**
+   * Forward: o = softmax(q k^T / sqrt(headDim)) v on [batch, numHeads, seq, headDim].
+   * saveStates keeps o and the row logsumexp for computeBackward.
+   */
+  Tensor<DType> computeAttention(const Tensor<DType>& queries, const Tensor<DType>& keys,
+                                 const Tensor<DType>& values, bool saveStates = false) {
+    const int batchSize = queries.shape()[0];
+    const int sequenceLength = queries.shape()[2];
+    const size_t rows = (size_t)batchSize * numHeads * sequenceLength;
+    Tensor<DType> output(queries.shape().toVector());
+    std::shared_ptr<float[]> lse = cudaMakeShared<float>(rows);
+    runForward(queries, keys, values, output.data(), lse.get(), batchSize, sequenceLength);
+    if (saveStates) {
+      cachedLSE = lse;
+      cachedMaxScores = cudaMakeShared<DType>(rows);
+      castKernel<float, DType><<<(rows + 255) / 256, 256>>>(lse.get(), cachedMaxScores.get(), rows);
+      cachedDenominators = cudaMakeShared<DType>(rows, (DType)1.0f);
+      cachedOutput = cudaCloneShared<DType>(output.dataPtr(), output.size());
+      cachedBatchSize = batchSize;
+      cachedSequenceLength = sequenceLength;
+    }
+    return output;
+  }
+
+  /**
+   * Backward: [dq, dk, dv] for the upstream gradient outputGrad.  Recomputes
+   * the forward when computeAttention did not save states.
+   */
+  std::array<Tensor<DType>, 3> computeBackward(const Tensor<DType>& queries, const Tensor<DType>& keys,
+                                               const Tensor<DType>& values, const Tensor<DType>& outputGrad) {
+    std::array<Tensor<DType>, 3> grads;
+    grads[0] = Tensor<DType>(queries.shape());
+    grads[1] = Tensor<DType>(keys.shape());
+    grads[2] = Tensor<DType>(values.shape());
+    const int batchSize = queries.shape()[0];
+    const int sequenceLength = queries.shape()[2];
+    const size_t rows = (size_t)batchSize * numHeads * sequenceLength;
+
+    std::shared_ptr<DType[]> output = cachedOutput;
+    std::shared_ptr<float[]> lse = cachedLSE;
+    if (output == nullptr || lse == nullptr || cachedBatchSize != batchSize ||
+        cachedSequenceLength != sequenceLength) {
+      output = cudaMakeShared<DType>(rows * headDim);
+      lse = cudaMakeShared<float>(rows);
+      runForward(queries, keys, values, output.get(), lse.get(), batchSize, sequenceLength);
+    }
+    const int code = ctfa_dropin::DtypeCode<DType>::value;
+    const size_t wsBytes = ctfa_backward_workspace_bytes(batchSize, numHeads, sequenceLength, headDim, code);
+    std::shared_ptr<unsigned char[]> ws = cudaMakeShared<unsigned char>(wsBytes > 0 ? wsBytes : 256);
+    ctfa_dropin::check(ctfa_backward(queries.get(), keys.get(), values.get(), output.get(), outputGrad.get(),
+                                     lse.get(), grads[0].data(), grads[1].data(), grads[2].data(), ws.get(),
+                                     wsBytes, batchSize, numHeads, sequenceLength, headDim, code, causal ? 1 : 0,
+                                     nullptr),
+                       "ctfa_backward");
+    return grads;
+  }
+
+  /** Clear cached values to free memory. */
+  void clearCache() {
+    cachedMaxScores = nullptr;
+    cachedDenominators = nullptr;
+    cachedOutput = nullptr;
+    cachedLSE = nullptr;
+  }
+
+ private:
+  void runForward(const Tensor<DType>& queries, const Tensor<DType>& keys, const Tensor<DType>& values,
+                  DType* output, float* lse, int batchSize, int sequenceLength) {
+    const int code = ctfa_dropin::DtypeCode<DType>::value;
+    const size_t wsBytes = ctfa_forward_workspace_bytes(batchSize, numHeads, sequenceLength, headDim, code);
+    std::shared_ptr<unsigned char[]> ws = wsBytes > 0 ? cudaMakeShared<unsigned char>(wsBytes) : nullptr;
+    ctfa_dropin::check(ctfa_forward(queries.get(), keys.get(), values.get(), output, lse, batchSize, numHeads,
+                                    sequenceLength, headDim, code, causal ? 1 : 0, ws.get(), wsBytes, nullptr),
+                       "ctfa_forward");
+  }
+};
+
+#endif  // FLASH_ATTENTION_LAYER

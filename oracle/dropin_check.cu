@@ -1,0 +1,43 @@
+// dropin_check.cu -- TEST INFRASTRUCTURE ONLY.  Compiles the reference's own
+// AttentionLayer / TransformerBlockLayer (cuda_transformer/*.cu, unmodified,
+// from the reference tree) against cudatransformer_b200/FlashAttentionLayer.cu,
+// for every element type the reference instantiates (float, double, half,
+// bfloat16; cuda_transformer.cu:839-842), and exposes one C entry point that
+// runs the reference's AttentionLayer<float>::forward through it.  It proves
+// the drop-in compiles where the reference's layer did, and lets a GPU test
+// compare the composed layer with an fp64 restatement.
+#include "FlashAttentionLayer.cu"  // ours: same include guard as the reference file
+#include "TransformerBlockLayer.cu"  // reference: pulls AttentionLayer.cu -> our layer
+
+template struct FlashAttentionLayer<float>;
+template struct FlashAttentionLayer<double>;
+template struct FlashAttentionLayer<__half>;
+template struct FlashAttentionLayer<__nv_bfloat16>;
+template struct AttentionLayer<float>;
+template struct AttentionLayer<__nv_bfloat16>;
+template struct TransformerBlockLayer<float>;
+
+// x: [B, N, E] host array; w*: [E, E] host arrays (row-major, y = x W^T);
+// out: [B, N, E] host array.  Biases are zero.  causal selects the mask.
+extern "C" int dropin_attention_forward(const float* x, const float* wq, const float* wk, const float* wv,
+                                        const float* wo, float* out, int B, int N, int E, int H, int causal) {
+  try {
+    const int D = E / H;
+    AttentionLayer<float> layer(E, H, D);
+    layer.flashAttn.causal = causal != 0;
+    auto load = [](const float* host, std::vector<size_t> shape) {
+      Tensor<float> t(shape);
+      cudaMemcpy(t.data(), host, t.size() * sizeof(float), cudaMemcpyHostToDevice);
+      return t;
+    };
+    layer.setQueryWeights(load(wq, {(size_t)E, (size_t)E}));
+    layer.setKeyWeights(load(wk, {(size_t)E, (size_t)E}));
+    layer.setValueWeights(load(wv, {(size_t)E, (size_t)E}));
+    layer.setOutputWeights(load(wo, {(size_t)E, (size_t)E}));
+    Tensor<float> y = layer.forward(load(x, {(size_t)B, (size_t)N, (size_t)E}));
+    cudaMemcpy(out, y.data(), y.size() * sizeof(float), cudaMemcpyDeviceToHost);
+    return (int)cudaDeviceSynchronize();
+  } catch (const std::exception&) {
+    return -1;
+  }
+}
