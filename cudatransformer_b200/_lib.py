@@ -27,6 +27,8 @@ CTFA_DTYPE_BF16 = 1
 CTFA_DTYPE_F16 = 2
 CTFA_DTYPE_F64 = 3
 
+CTFA_NOALLOC_SCRATCH_BYTES = 32 << 20
+
 _c_void_p = ctypes.c_void_p
 _c_int = ctypes.c_int
 _c_size_t = ctypes.c_size_t
@@ -51,6 +53,10 @@ SIGNATURES = {
     "ctfa_backward_with_events": (
         _c_int,
         [_c_void_p] * 10 + [_c_size_t] + [_c_int] * 6 + [_c_void_p, _c_void_p],
+    ),
+    "ctfa_backward_noalloc": (
+        _c_int,
+        [_c_void_p] * 9 + [_c_int] * 6 + [_c_void_p],
     ),
     "ctfa_set_wait_limit_ns": (_c_int, [_c_ull]),
     "ctfa_check_device_error": (_c_int, [_c_void_p]),

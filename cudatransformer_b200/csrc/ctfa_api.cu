@@ -560,6 +560,59 @@ extern "C" int ctfa_backward_with_events(const void* q, const void* k, const voi
                        reinterpret_cast<cudaEvent_t*>(events));
 }
 
+// ---------------------------------------------------------------------------
+// Backward without allocation: scratch in a static device array.
+// ---------------------------------------------------------------------------
+namespace {
+
+// Scratch of ctfa_backward_noalloc.  Static device memory: every GPU that
+// loads this library holds these CTFA_NOALLOC_SCRATCH_BYTES until exit.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[CTFA_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 128;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device.  In host code
+// the array's name is only a host-side stand-in, so the address is looked up
+// once per device (with that device current) and cached.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(CTFA_ERR_UNSUPPORTED, "device index out of range");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return CTFA_OK;
+}
+
+}  // namespace
+
+extern "C" int ctfa_backward_noalloc(const void* q, const void* k, const void* v, const void* o, const void* dO,
+                                     const float* lse, void* dq, void* dk, void* dv, int B, int H, int T, int D,
+                                     int dtype, int causal, void* stream) {
+  int s = check_common(B, H, T, D, dtype);
+  if (s != CTFA_OK) return s;
+  if (!q || !k || !v || !o || !dO || !lse || !dq || !dk || !dv)
+    return fail(CTFA_ERR_INVALID_ARGUMENT, "q, k, v, o, dO, lse, dq, dk and dv must be non-null");
+  Problem pr = full_problem(B, H, T, D, dtype, causal);
+  const size_t need = bwd_workspace(pr);
+  if (need > CTFA_NOALLOC_SCRATCH_BYTES)
+    return fail(CTFA_ERR_WORKSPACE, "ctfa_backward_noalloc: this problem needs " + std::to_string(need) +
+                                        " bytes of scratch, the static scratch holds " +
+                                        std::to_string(CTFA_NOALLOC_SCRATCH_BYTES) +
+                                        "; call ctfa_backward with a caller-provided workspace");
+  void* ws = nullptr;
+  if ((s = noalloc_scratch(&ws)) != CTFA_OK) return s;
+  return backward_impl(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, (cudaStream_t)stream);
+}
+
 extern "C" int ctfa_check_device_error(void* stream) {
   cudaError_t e = cudaStreamSynchronize((cudaStream_t)stream);
   if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");

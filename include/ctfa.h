@@ -101,6 +101,31 @@ int ctfa_backward_with_events(const void* q, const void* k, const void* v, const
                               void* stream, void** events);
 
 /*
+ * Backward that allocates nothing.  No counterpart in the reference (its
+ * FlashAttentionLayer::computeBackward always allocates).  It exists for
+ * callers that cannot call cudaMalloc while they run attention: a serving or
+ * plugin host that has already handed all device memory to its own pool (so
+ * a new allocation fails or breaks its accounting), or a caller that cannot
+ * afford the device-wide synchronisation cudaMalloc may imply.  Same inputs,
+ * outputs and results as ctfa_backward, but the scratch (delta rows and, for
+ * fp32 I/O, the tf32-rounded operand copies) lives in a static device array
+ * of CTFA_NOALLOC_SCRATCH_BYTES inside this library, which every GPU that
+ * loads the library holds until the process exits.  Problems whose
+ * ctfa_backward_workspace_bytes(...) exceed that size are rejected with
+ * CTFA_ERR_WORKSPACE before anything is launched.
+ *   - The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress, with that device current); make that first call
+ *     before any stream capture on the device.
+ *   - All calls share the one array and leave their contents in it; calls
+ *     that overlap on the GPU (two streams, two host threads) race and must
+ *     be serialised by the caller.  Nothing in the array needs to start at zero.
+ */
+#define CTFA_NOALLOC_SCRATCH_BYTES (32ull << 20)
+int ctfa_backward_noalloc(const void* q, const void* k, const void* v, const void* o, const void* dO,
+                          const float* lse, void* dq, void* dk, void* dv, int B, int H, int T, int D, int dtype,
+                          int causal, void* stream);
+
+/*
  * Bound, in nanoseconds, on every wait inside the kernels (default 2e9).  A
  * kernel that waits longer records CTFA_ERR_DEVICE_TIMEOUT in a device error
  * word and exits without touching its outputs further.
