@@ -245,9 +245,20 @@ def run_ours(args, w):
         _lib.check(lib.ctfa_forward(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
                                     B, H, T, D, code, causal, fws.data_ptr(), fws.numel(), sh), "ctfa_forward")
 
+    # fp32: the backward reads the tf32-rounded q, k, v the forward left in its
+    # workspace (what FlashAttentionLayer does with saveStates), so it only
+    # rounds dO.
+    if fws_bytes:
+        qb, kb, vb = _lib.rounded_copies(fws, B, H, T, D)
+        bcode = _lib.CTFA_DTYPE_TF32
+        bws = torch.empty(lib.ctfa_backward_workspace_bytes(B, H, T, D, bcode), dtype=torch.uint8, device=dev)
+    else:
+        qb, kb, vb, bcode, bws = q.data_ptr(), k.data_ptr(), v.data_ptr(), code, ws
+
     def bwd(events=None):
-        ptrs = (q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(), lse.data_ptr(),
-                dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), ws.data_ptr(), ws.numel(), B, H, T, D, code, causal, sh)
+        ptrs = (qb, kb, vb, o.data_ptr(), do.data_ptr(), lse.data_ptr(),
+                dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), bws.data_ptr(), bws.numel(), B, H, T, D, bcode, causal,
+                sh)
         if events is None:
             _lib.check(lib.ctfa_backward(*ptrs), "ctfa_backward")
         else:
@@ -367,7 +378,7 @@ def run_ours(args, w):
         "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": 4 * nbytes,
                 "d2h_bytes_per_step": 4 * nbytes, "ms_per_step": round(ms_e2e / args.steps, 4),
                 "path": "ctfa_forward + ctfa_backward (C ABI) with pinned host buffers"},
-        "gpu_launches": 4 * args.steps,
+        "gpu_launches": (5 if fws_bytes else 4) * args.steps,
         "roofline": {"kernel": dom, "bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1),
                      "unit": "TFLOP/s", "frac": round(achieved / peak, 3) if peak else None,
                      "peak_source": peak_note, "flops_per_launch": kflops[dom],

@@ -26,6 +26,7 @@ CTFA_DTYPE_F32 = 0
 CTFA_DTYPE_BF16 = 1
 CTFA_DTYPE_F16 = 2
 CTFA_DTYPE_F64 = 3
+CTFA_DTYPE_TF32 = 4
 
 CTFA_NOALLOC_SCRATCH_BYTES = 32 << 20
 
@@ -104,6 +105,13 @@ def last_error() -> str:
 def check(status: int, where: str) -> None:
     if status != CTFA_OK:
         raise CtfaError(status, where, last_error())
+
+
+def rounded_copies(ws, B: int, H: int, T: int, D: int):
+    """Byte offsets of the tf32-rounded q, k, v that an fp32 ctfa_forward
+    leaves in its workspace (include/ctfa.h)."""
+    a = (B * H * T * D * 4 + 255) // 256 * 256
+    return [ws.data_ptr() + i * a for i in range(3)]
 
 
 def sync_check_enabled() -> bool:

@@ -35,26 +35,29 @@
 namespace ctfa {
 
 struct BwdPrepParams {
-  long long rows;    // BH * Tq
-  int Tq;
+  long long rows;    // BH * Tq_pad
+  int Tq, Tq_pad;    // rows per head, and rounded up to a whole 128-row tile
   int q_rows_alloc;
   int q_row0;
   const void* o;
   const void* dO;
-  float* delta;      // [BH][Tq]
+  const float* lse;  // [BH][q_rows_alloc] natural log
+  float* delta;      // [BH][Tq_pad]; 0 on padding rows
+  float* lse2;       // [BH][Tq_pad] lse * log2(e); +inf on padding rows (their P is 0)
   float* dO_round;   // fp32 I/O only: round-to-nearest tf32 copy of dO (nullable)
 };
 
 struct BwdParams {
   int BH;
   int Tq, Tk;
+  int Tq_pad;        // row stride of lse2 / delta
   int q_row0, k_row0;
   int q_rows_alloc, k_rows_alloc;
   int causal, causal_offset;
   float scale;       // 1/sqrt(D)
   float scale_log2;  // log2(e)/sqrt(D)
-  const float* lse;  // [BH][q_rows_alloc]
-  const float* delta;  // [BH][Tq]
+  const float* lse2;   // [BH][Tq_pad] lse * log2(e), +inf on padding rows
+  const float* delta;  // [BH][Tq_pad], 0 on padding rows
   void* dq;          // [BH][q_rows_alloc][HD]
   void* dk;          // [BH][k_rows_alloc][HD]
   void* dv;
@@ -80,7 +83,14 @@ __global__ void __launch_bounds__(256) attn_bwd_prep(BwdPrepParams p) {
   const long long w = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (w >= p.rows) return;
-  const long long bh = w / p.Tq, i = w % p.Tq;
+  const long long bh = w / p.Tq_pad, i = w % p.Tq_pad;
+  if (i >= p.Tq) {  // padding row of the last tile
+    if (lane == 0) {
+      p.delta[w] = 0.f;
+      p.lse2[w] = INFINITY;
+    }
+    return;
+  }
   const size_t row = ((size_t)bh * p.q_rows_alloc + p.q_row0 + i) * HD;
   const DT* o = reinterpret_cast<const DT*>(p.o) + row;
   const DT* g = reinterpret_cast<const DT*>(p.dO) + row;
@@ -104,7 +114,10 @@ __global__ void __launch_bounds__(256) attn_bwd_prep(BwdPrepParams p) {
   }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-  if (lane == 0) p.delta[w] = s;
+  if (lane == 0) {
+    p.delta[w] = s;
+    p.lse2[w] = p.lse[bh * p.q_rows_alloc + p.q_row0 + i] * 1.4426950408889634f;
+  }
 }
 
 
@@ -170,13 +183,8 @@ struct BwdConfig {
 template <int N>
 __device__ __forceinline__ void tmem_load_row(uint32_t taddr, float (&v)[N]) {
 #pragma unroll
-  for (int c = 0; c < N / 32; ++c) {
-    uint32_t regs[32];
-    tmem_ld32(taddr + c * 32, regs);
-    tmem_wait_ld();
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[c * 32 + i] = __uint_as_float(regs[i]);
-  }
+  for (int c = 0; c < N / 32; ++c) tmem_ld32f(taddr + c * 32, v + c * 32);
+  tmem_wait_ld();
 }
 
 // Store v[] as an MMA A operand: tf32 (one column per value, rounded to
@@ -431,42 +439,73 @@ __global__ void __launch_bounds__(320, 1)
     const bool key_ok = key < p.Tk;
     const float sl2 = p.scale_log2;
     const float scale = p.scale;
-    const float* lse_bh = p.lse + (size_t)bh * p.q_rows_alloc + p.q_row0;
-    const float* delta_bh = p.delta + (size_t)bh * p.Tq;
+    // lse*log2(e) and delta for this head, padded to whole tiles (+inf / 0 on
+    // padding rows), 16-byte aligned: whole float4 loads, no bounds checks.
+    const float* lse2_bh = p.lse2 + (size_t)bh * p.Tq_pad;
+    const float* delta_bh = p.delta + (size_t)bh * p.Tq_pad;
     bool ok = true;
     for (int it = 0; it < n_it; ++it) {
-      const int q0 = (qt_first + it) * QT + h * HALF;
+      const int qtile0 = (qt_first + it) * QT;
+      const int q0 = qtile0 + h * HALF;
+      float L[HALF];
+#pragma unroll
+      for (int c = 0; c < HALF / 4; ++c) {
+        const float4 v4 = __ldg(reinterpret_cast<const float4*>(lse2_bh + q0) + c);
+        L[4 * c] = v4.x;
+        L[4 * c + 1] = v4.y;
+        L[4 * c + 2] = v4.z;
+        L[4 * c + 3] = v4.w;
+      }
       if (!(ok = mbar_wait(s_full, it & 1, abort_flag, limit, 17))) break;
       tc_fence_after();
       float s[HALF];
       tmem_load_row(tbase + lane_off + C::KV_S + h * HALF, s);
       tc_fence_before();
       mbar_arrive(s_free);
-      // P^T = exp2(S^T * scale*log2e - lse*log2e), masked
+      // P^T = exp2(S^T * scale*log2e - lse*log2e); padding queries have lse = +inf
 #pragma unroll
-      for (int c = 0; c < HALF; ++c) {
-        const int q = q0 + c;
-        const bool vis = key_ok && q < p.Tq && (!p.causal || key <= q + p.causal_offset);
-        const float L = vis ? __ldg(lse_bh + q) * 1.4426950408889634f : 0.f;
-        s[c] = vis ? ex2_approx(fmaf(s[c], sl2, -L)) : 0.f;
+      for (int c = 0; c < HALF; ++c) s[c] = ex2_approx(fmaf(s[c], sl2, -L[c]));
+      // causal diagonal tile / keys past Tk: zero the invisible entries
+      if (!key_ok) {
+#pragma unroll
+        for (int c = 0; c < HALF; ++c) s[c] = 0.f;
+      } else if (p.causal && key0 + C::KV_KEYS - 1 > qtile0 + p.causal_offset) {
+        const int cmin = key - p.causal_offset - q0;  // first visible column
+#pragma unroll
+        for (int c = 0; c < HALF; ++c)
+          if (c < cmin) s[c] = 0.f;
       }
       if (!(ok = mbar_wait(dp_full, it & 1, abort_flag, limit, 18))) break;
       tc_fence_after();
-      float dsv[HALF];
-      tmem_load_row(tbase + lane_off + C::KV_DP + h * HALF, dsv);
+      // dS^T = P^T (dP^T - delta) * scale, 32 columns at a time, written in
+      // place (tf32) or packed into the already-read front of the dP buffer.
 #pragma unroll
-      for (int c = 0; c < HALF; ++c) {
-        const int q = q0 + c;
-        const float dl = q < p.Tq ? __ldg(delta_bh + q) : 0.f;
-        dsv[c] = s[c] * (dsv[c] - dl) * scale;
+      for (int ch = 0; ch < HALF / 32; ++ch) {
+        float dsv[32];
+        {
+          uint32_t regs[32];
+          tmem_ld32(tbase + lane_off + C::KV_DP + h * HALF + ch * 32, regs);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c4 = 0; c4 < 8; ++c4) {
+            const float4 d4 = __ldg(reinterpret_cast<const float4*>(delta_bh + q0 + ch * 32) + c4);
+            const float dd[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int i = 4 * c4 + e;
+              dsv[i] = s[ch * 32 + i] * (__uint_as_float(regs[i]) - dd[e]) * scale;
+            }
+          }
+        }
+        if constexpr (C::TF32)
+          tmem_store_operand<DT>(tbase + lane_off + C::KV_DP + h * HALF + ch * 32, dsv);
+        else
+          tmem_store_operand<DT>(tbase + lane_off + C::KV_DP + h * HALF + ch * 16, dsv);
       }
-      if constexpr (C::TF32) {
+      if constexpr (C::TF32)
         tmem_store_operand<DT>(tbase + lane_off + C::KV_P + h * HALF, s);
-        tmem_store_operand<DT>(tbase + lane_off + C::KV_DP + h * HALF, dsv);
-      } else {
+      else
         tmem_store_operand<DT>(tbase + lane_off + C::KV_DP + h * HALF + HALF / 2, s);
-        tmem_store_operand<DT>(tbase + lane_off + C::KV_DP + h * HALF, dsv);
-      }
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(p_full);
@@ -687,8 +726,8 @@ __global__ void __launch_bounds__(320, 1)
     const float sl2 = p.scale_log2;
     const float scale = p.scale;
     const size_t lrow = (size_t)bh * p.q_rows_alloc + p.q_row0 + q;
-    const float L = q_ok ? p.lse[lrow] * 1.4426950408889634f : 0.f;
-    const float dl = q_ok ? p.delta[(size_t)bh * p.Tq + q] : 0.f;
+    const float L = q_ok ? p.lse2[(size_t)bh * p.Tq_pad + q] : 0.f;
+    const float dl = q_ok ? p.delta[(size_t)bh * p.Tq_pad + q] : 0.f;
     int vis = p.Tk - 1;
     if (p.causal) vis = min(vis, q + p.causal_offset);
     if (!q_ok) vis = -1;
@@ -701,9 +740,14 @@ __global__ void __launch_bounds__(320, 1)
       tmem_load_row(tbase + lane_off + C::Q_S + h * HALF, s);
       tc_fence_before();
       mbar_arrive(s_free);
-      const int lim = vis - kc0;
+      const int lim = vis - kc0;  // columns > lim are masked (diagonal / tail tiles only)
 #pragma unroll
-      for (int c = 0; c < HALF; ++c) s[c] = (c <= lim) ? ex2_approx(fmaf(s[c], sl2, -L)) : 0.f;
+      for (int c = 0; c < HALF; ++c) s[c] = ex2_approx(fmaf(s[c], sl2, -L));
+      if (lim < HALF - 1) {
+#pragma unroll
+        for (int c = 0; c < HALF; ++c)
+          if (c > lim) s[c] = 0.f;
+      }
       if (!(ok = mbar_wait(dp_full, j & 1, abort_flag, limit, 31))) break;
       tc_fence_after();
       float dsv[HALF];

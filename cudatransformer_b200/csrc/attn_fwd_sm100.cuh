@@ -12,6 +12,8 @@
 //                     query row (= TMEM lane).
 //   warp  4*NQ      : TMA producer (Q once, then K/V tiles through ST stages).
 //   warp  4*NQ+1    : tcgen05.mma issuer (one elected lane).
+//   warps 4*NQ+2,3  : spare (they complete the producer warpgroup, which hands
+//                     its registers to the softmax warpgroups via setmaxnreg).
 //
 //   V is the MN-major B operand of P V: 128B swizzle for 16-bit types, the
 //   32-byte-granule variant for tf32.
@@ -64,14 +66,22 @@ struct FwdConfig {
   static constexpr uint32_t TMEM_COLS = tmem_cols_for(NQ * (BN + HD));
   static constexpr int NUM_BARS = 1 + 4 * ST + 3 * NQ + 1;
   static constexpr int SMEM_BYTES = 1024 + NQ * Q_TILE_BYTES + 2 * ST * KV_TILE_BYTES + NUM_BARS * 8 + 16;
-  static constexpr int THREADS = NQ * 128 + 64;
+  // NQ softmax warpgroups + one producer warpgroup (TMA warp, MMA warp, two
+  // spare warps) so that registers can be rebalanced per warpgroup.
+  static constexpr int THREADS = NQ * 128 + 128;
+  // With NQ = 2 the block launches at 168 registers/thread (3 warps per SMSP):
+  // 384 * 168 = 64512 = 256 * 224 (softmax) + 128 * 56 (producer).
+  static constexpr bool REBALANCE = (NQ == 2);
+  static constexpr int SOFTMAX_REGS = 224;
+  static constexpr int PRODUCER_REGS = 56;
+  static_assert(!REBALANCE || 256 * SOFTMAX_REGS + 128 * PRODUCER_REGS <= 384 * 168, "register split");
   static_assert(HD * EB % 128 == 0, "head dim must fill whole 128-byte rows");
   static_assert(BN % 32 == 0 && BN <= 256, "key tile");
   static_assert(NQ * (BN + HD) <= 512, "TMEM budget");
 };
 
 template <typename DT, int HD, int NQ, int BN, int ST>
-__global__ void __launch_bounds__(NQ * 128 + 64, 1)
+__global__ void __launch_bounds__(NQ * 128 + 128, 1)
     attn_fwd_sm100(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
   using C = FwdConfig<DT, HD, NQ, BN, ST>;
@@ -156,6 +166,9 @@ __global__ void __launch_bounds__(NQ * 128 + 64, 1)
   const uint32_t tbase = *tmem_holder;
   const uint64_t limit = p.wait_limit_ns;
 
+  if (warp >= NQ * 4) {
+    // --------------------------- producer warpgroup ---------------------------
+    if constexpr (C::REBALANCE) regs_decrease<C::PRODUCER_REGS>();
   if (warp == TMA_WARP) {
     if (lane == 0 && n_max > 0) {
       tma_prefetch_desc(&tm_q);
@@ -279,8 +292,10 @@ __global__ void __launch_bounds__(NQ * 128 + 64, 1)
       }
     }
     __syncwarp();
+  }  // spare warps of the producer warpgroup have no role
   } else {
     // ---------------------------- softmax warps ----------------------------
+    if constexpr (C::REBALANCE) regs_increase<C::SOFTMAX_REGS>();
     const int k = threadIdx.x >> 7;          // query tile inside the CTA
     const int r = threadIdx.x & 127;         // row inside the tile (TMEM lane)
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
@@ -296,15 +311,6 @@ __global__ void __launch_bounds__(NQ * 128 + 64, 1)
     for (int j = 0; j < n; ++j) {
       if (!(ok = mbar_wait(&s_full[k], j & 1, abort_flag, limit, 8))) break;
       tc_fence_after();
-      float s[BN];
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t regs[32];
-        tmem_ld32(s_addr + c * 32, regs);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(regs[i]);
-      }
       const int key0 = j * BN;
       int vis = p.Tk - 1;  // last visible key for this row
       int vis_tile = p.Tk - 1;
@@ -312,16 +318,25 @@ __global__ void __launch_bounds__(NQ * 128 + 64, 1)
         vis = min(vis, q_local + p.causal_offset);
         vis_tile = min(vis_tile, qt * BM + p.causal_offset);
       }
-      if (key0 + BN - 1 > vis_tile) {
-        const int lim = vis - key0;
+      const bool need_mask = key0 + BN - 1 > vis_tile;  // only diagonal / last tiles
+      float sv[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) tmem_ld32f(s_addr + c * 32, sv + c * 32);
+      tmem_wait_ld();
+      if (need_mask) {
+        const int lim = vis - key0;  // columns > lim are masked
 #pragma unroll
         for (int c = 0; c < BN; ++c)
-          if (c > lim) s[c] = -INFINITY;
+          if (c > lim) sv[c] = -INFINITY;
       }
-      float mx = -INFINITY;
+      // row max: four independent chains
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int c = 0; c < BN; ++c) mx = fmaxf(mx, s[c]);
-      mx *= sl2;
+      for (int c = 0; c < BN; c += 4) {
+#pragma unroll
+        for (int t = 0; t < 4; ++t) mx4[t] = fmaxf(mx4[t], sv[c + t]);
+      }
+      float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
       if (j == 0) {
         m = mx;
       } else {
@@ -333,43 +348,52 @@ __global__ void __launch_bounds__(NQ * 128 + 64, 1)
           m = m_new;
 #pragma unroll
           for (int c = 0; c < HD / 32; ++c) {
-            uint32_t regs[32];
-            tmem_ld32(o_addr + c * 32, regs);
+            float o[32];
+            tmem_ld32f(o_addr + c * 32, o);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) regs[i] = __float_as_uint(__uint_as_float(regs[i]) * alpha);
-            tmem_st32(o_addr + c * 32, regs);
+            for (int i = 0; i < 32; ++i) o[i] *= alpha;
+            tmem_st32f(o_addr + c * 32, o);
           }
         }
       }
       const float m_use = (m == -INFINITY) ? 0.f : m;
-      float rs = 0.f;
+      // p = exp2(s * scale*log2e - m): packed fp32x2 FMA, two row-sum chains;
+      // masked columns hold -inf and give exactly 0.
+      const float2 sl2x2 = make_float2(sl2, sl2);
+      const float2 negm = make_float2(-m_use, -m_use);
+      float2 rs2a = make_float2(0.f, 0.f), rs2b = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int c = 0; c < BN; ++c) {
-        s[c] = ex2_approx(fmaf(s[c], sl2, -m_use));
-        rs += s[c];
+      for (int c = 0; c < BN; c += 4) {
+        float2 y0 = __ffma2_rn(make_float2(sv[c], sv[c + 1]), sl2x2, negm);
+        float2 y1 = __ffma2_rn(make_float2(sv[c + 2], sv[c + 3]), sl2x2, negm);
+        y0.x = ex2_approx(y0.x);
+        y0.y = ex2_approx(y0.y);
+        y1.x = ex2_approx(y1.x);
+        y1.y = ex2_approx(y1.y);
+        sv[c] = y0.x;
+        sv[c + 1] = y0.y;
+        sv[c + 2] = y1.x;
+        sv[c + 3] = y1.y;
+        rs2a = __fadd2_rn(rs2a, y0);
+        rs2b = __fadd2_rn(rs2b, y1);
       }
-      l += rs;
+      l += (rs2a.x + rs2a.y) + (rs2b.x + rs2b.y);
+      // P over the S columns: tf32 (rounded to nearest) in place, or packed pairs.
       if constexpr (C::EB == 4) {
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t regs[32];
+        for (int c = 0; c < BN; ++c) sv[c] = __uint_as_float(f32_to_tf32_rna(sv[c]));
 #pragma unroll
-          for (int i = 0; i < 32; ++i) regs[i] = f32_to_tf32_rna(s[c * 32 + i]);
-          tmem_st32(s_addr + c * 32, regs);
-        }
+        for (int c = 0; c < BN / 32; ++c) tmem_st32f(s_addr + c * 32, sv + c * 32);
       } else {
 #pragma unroll
-        for (int c = 0; c < BN / 64; ++c) {
-          uint32_t regs[32];
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t regs[16];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            if constexpr (kFmt == 1)
-              regs[i] = pack_bf16x2(s[c * 64 + 2 * i], s[c * 64 + 2 * i + 1]);
-            else
-              regs[i] = pack_f16x2(s[c * 64 + 2 * i], s[c * 64 + 2 * i + 1]);
-          }
-          tmem_st32(s_addr + c * 32, regs);
+          for (int i = 0; i < 16; ++i)
+            regs[i] = (kFmt == 1) ? pack_bf16x2(sv[c * 32 + 2 * i], sv[c * 32 + 2 * i + 1])
+                                  : pack_f16x2(sv[c * 32 + 2 * i], sv[c * 32 + 2 * i + 1]);
+          tmem_st16(s_addr + c * 16, regs);
         }
       }
       tmem_wait_st();

@@ -42,6 +42,7 @@ size_t dtype_bytes(int dtype) {
     case CTFA_DTYPE_BF16: return 2;
     case CTFA_DTYPE_F16: return 2;
     case CTFA_DTYPE_F64: return 8;
+    case CTFA_DTYPE_TF32: return 4;
     default: return 0;
   }
 }
@@ -73,7 +74,7 @@ int make_map(CUtensorMap* map, const void* base, int dtype, int D, int rows, int
   auto fn = encode_fn();
   if (!fn) return fail(CTFA_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
   const size_t eb = dtype_bytes(dtype);
-  CUtensorMapDataType dt = dtype == CTFA_DTYPE_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+  CUtensorMapDataType dt = (dtype == CTFA_DTYPE_F32 || dtype == CTFA_DTYPE_TF32) ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                            : dtype == CTFA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)rows, (cuuint64_t)BH};
@@ -110,7 +111,8 @@ struct Problem {
 };
 
 bool tensor_core_shape(const Problem& pr) {
-  return (pr.dtype == CTFA_DTYPE_F32 || pr.dtype == CTFA_DTYPE_BF16 || pr.dtype == CTFA_DTYPE_F16) &&
+  return (pr.dtype == CTFA_DTYPE_F32 || pr.dtype == CTFA_DTYPE_TF32 || pr.dtype == CTFA_DTYPE_BF16 ||
+          pr.dtype == CTFA_DTYPE_F16) &&
          (pr.D == 64 || pr.D == 128);
 }
 
@@ -250,6 +252,9 @@ int forward_impl(const Problem& pr, const void* q, const void* k, const void* v,
         return pr.D == 64 ? launch_fwd_tc<float, 64, 2, 128, 2>(pr, r[0], r[1], r[2], o, lse, stream)
                           : launch_fwd_tc<float, 128, 1, 64, 2>(pr, r[0], r[1], r[2], o, lse, stream);
       }
+      case CTFA_DTYPE_TF32:
+        return pr.D == 64 ? launch_fwd_tc<float, 64, 2, 128, 2>(pr, q, k, v, o, lse, stream)
+                          : launch_fwd_tc<float, 128, 1, 64, 2>(pr, q, k, v, o, lse, stream);
       case CTFA_DTYPE_BF16:
         return pr.D == 64 ? launch_fwd_tc<__nv_bfloat16, 64, 2, 128, 3>(pr, q, k, v, o, lse, stream)
                           : launch_fwd_tc<__nv_bfloat16, 128, 2, 128, 2>(pr, q, k, v, o, lse, stream);
@@ -259,7 +264,8 @@ int forward_impl(const Problem& pr, const void* q, const void* k, const void* v,
     }
   }
   switch (pr.dtype) {
-    case CTFA_DTYPE_F32: return launch_fwd_simt<float>(pr, q, k, v, o, lse, stream);
+    case CTFA_DTYPE_F32:
+    case CTFA_DTYPE_TF32: return launch_fwd_simt<float>(pr, q, k, v, o, lse, stream);
     case CTFA_DTYPE_BF16: return launch_fwd_simt<__nv_bfloat16>(pr, q, k, v, o, lse, stream);
     case CTFA_DTYPE_F16: return launch_fwd_simt<__half>(pr, q, k, v, o, lse, stream);
     default: return launch_fwd_simt<double>(pr, q, k, v, o, lse, stream);
@@ -291,12 +297,19 @@ Problem full_problem(int B, int H, int T, int D, int dtype, int causal) {
 // ---------------------------------------------------------------------------
 // Backward
 // ---------------------------------------------------------------------------
+// Rows of the padded per-row arrays of the tensor-core backward: each head's
+// rows rounded up to a whole 128-row tile, so tiles read them with aligned
+// vector loads and without bounds checks.
+size_t padded_tq(const Problem& pr) { return (size_t)((pr.Tq + 127) / 128) * 128; }
+size_t padded_rows(const Problem& pr) { return (size_t)pr.B * pr.H * padded_tq(pr); }
+
 size_t bwd_workspace(const Problem& pr) {
   const size_t rows = (size_t)pr.B * pr.H * pr.Tq;
-  if (tensor_core_shape(pr)) {
-    size_t ws = align256(rows * sizeof(float));  // delta
-    if (needs_rounding(pr.dtype, pr.D) && pr.D == 64)  // rounded q, k, v, dO (fp32 D=128 runs SIMT)
-      ws += 4 * align256(rows * pr.D * sizeof(float));
+  if (tensor_core_shape(pr) && !(pr.D == 128 && (pr.dtype == CTFA_DTYPE_F32 || pr.dtype == CTFA_DTYPE_TF32))) {
+    size_t ws = 2 * align256(padded_rows(pr) * sizeof(float));  // delta, lse*log2(e) (padded rows)
+    const size_t n = align256(rows * pr.D * sizeof(float));
+    if (pr.dtype == CTFA_DTYPE_F32) ws += 4 * n;   // rounded q, k, v, dO
+    if (pr.dtype == CTFA_DTYPE_TF32) ws += n;      // rounded dO
     return ws;
   }
   if (pr.dtype == CTFA_DTYPE_F64) return 2 * align256(rows * sizeof(double));  // delta + lse in double
@@ -342,9 +355,14 @@ int launch_bwd_tc(const Problem& pr, const void* q, const void* k, const void* v
   const int BH = pr.B * pr.H;
   float* delta = reinterpret_cast<float*>(ws);
   // 1. delta = rowsum(O * dO)
+  const int Tq_pad = (int)padded_tq(pr);
+  float* lse2 = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + align256(padded_rows(pr) * sizeof(float)));
   BwdPrepParams pp;
-  pp.rows = (long long)BH * pr.Tq;
+  pp.rows = (long long)BH * Tq_pad;
   pp.Tq = pr.Tq;
+  pp.Tq_pad = Tq_pad;
+  pp.lse = lse;
+  pp.lse2 = lse2;
   pp.q_rows_alloc = pr.q_rows;
   pp.q_row0 = pr.q_row0;
   pp.o = o;
@@ -390,7 +408,8 @@ int launch_bwd_tc(const Problem& pr, const void* q, const void* k, const void* v
   p.causal_offset = pr.causal_offset;
   p.scale = (float)(1.0 / std::sqrt((double)HD));
   p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)HD));
-  p.lse = lse;
+  p.Tq_pad = Tq_pad;
+  p.lse2 = lse2;
   p.delta = delta;
   p.dq = dq;
   p.dk = dk;
@@ -430,13 +449,15 @@ int backward_impl(const Problem& pr, const void* q, const void* k, const void* v
       return fail(CTFA_ERR_MISALIGNED, "q/k/v/o/dO/dq/dk/dv must be 16-byte aligned");
     switch (pr.dtype) {
       case CTFA_DTYPE_F32:
+      case CTFA_DTYPE_TF32:
         if (pr.D == 64) {
-          const size_t rows = (size_t)pr.B * pr.H * pr.Tq;
-          const size_t n = rows * pr.D;
-          char* w = reinterpret_cast<char*>(ws) + align256(rows * sizeof(float));
+          const size_t n = (size_t)pr.B * pr.H * pr.Tq * pr.D;
+          char* w = reinterpret_cast<char*>(ws) + 2 * align256(padded_rows(pr) * sizeof(float));
+          record(ev, 0, stream);
+          if (pr.dtype == CTFA_DTYPE_TF32)  // q, k, v already rounded; the delta pass rounds dO into w
+            return launch_bwd_tc<float, 64>(pr, q, k, v, o, dO, w, lse, dq, dk, dv, ws, stream, ev);
           void* r[4] = {w, w + align256(n * 4), w + 2 * align256(n * 4), w + 3 * align256(n * 4)};
           const void* in[3] = {q, k, v};
-          record(ev, 0, stream);
           if ((s = launch_round(in, r, 3, n, stream)) != CTFA_OK) return s;
           // the delta pass writes the rounded dO (r[3]) the GEMMs read
           return launch_bwd_tc<float, 64>(pr, r[0], r[1], r[2], o, dO, r[3], lse, dq, dk, dv, ws, stream, ev);
@@ -451,7 +472,8 @@ int backward_impl(const Problem& pr, const void* q, const void* k, const void* v
     }
   }
   switch (pr.dtype) {
-    case CTFA_DTYPE_F32: return launch_bwd_simt<float>(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, stream, ev);
+    case CTFA_DTYPE_F32:
+    case CTFA_DTYPE_TF32: return launch_bwd_simt<float>(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, stream, ev);
     case CTFA_DTYPE_BF16: return launch_bwd_simt<__nv_bfloat16>(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, stream, ev);
     case CTFA_DTYPE_F16: return launch_bwd_simt<__half>(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, stream, ev);
     default: return launch_bwd_simt<double>(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, stream, ev);

@@ -20,6 +20,10 @@ Differences from the reference, all deliberate:
     ones, so ``exp(s - max) / denom`` still gives the softmax.
   * dK and dV are the exact gradients (the reference kernel's are not,
     flash_attention.cu:310-321).
+  * fp32: the forward rounds q, k, v to tf32 into a workspace; with saveStates
+    that workspace is kept with the other cached state, and computeBackward
+    reuses it (CTFA_DTYPE_TF32) when it is called on the same, unmodified
+    q, k, v tensors.
 """
 from __future__ import annotations
 
@@ -55,6 +59,7 @@ class FlashAttentionLayer:
         self.cachedDenominators: torch.Tensor | None = None
         self.cachedOutput: torch.Tensor | None = None
         self.cachedLSE: torch.Tensor | None = None
+        self._cachedRounded = None  # (workspace, identity of q, k, v) for fp32
         self.cachedBatchSize = 0
         self.cachedSequenceLength = 0
 
@@ -95,6 +100,11 @@ class FlashAttentionLayer:
             _lib.check(status, "ctfa_forward")
             if _lib.sync_check_enabled():
                 _lib.check(lib.ctfa_check_device_error(_stream_handle(q.device)), "ctfa_forward (device)")
+        return ws
+
+    @staticmethod
+    def _identity(*tensors):
+        return tuple((t.data_ptr(), t._version) for t in tensors)
 
     # -- API -------------------------------------------------------------
     def computeAttention(
@@ -104,8 +114,9 @@ class FlashAttentionLayer:
         lib = _lib.load()
         output = torch.empty_like(queries)
         lse = torch.empty((B, self.numHeads, T), dtype=torch.float32, device=queries.device)
-        self._forward(lib, queries, keys, values, output, lse, B, T, dt)
+        ws = self._forward(lib, queries, keys, values, output, lse, B, T, dt)
         if saveStates:
+            self._cachedRounded = (ws, self._identity(queries, keys, values)) if ws is not None else None
             self.cachedLSE = lse
             self.cachedMaxScores = lse.to(queries.dtype)
             self.cachedDenominators = torch.ones_like(self.cachedMaxScores)
@@ -129,11 +140,17 @@ class FlashAttentionLayer:
         dq = torch.empty_like(queries)
         dk = torch.empty_like(keys)
         dv = torch.empty_like(values)
+        q_ptr, k_ptr, v_ptr = _ptr(queries), _ptr(keys), _ptr(values)
+        cached = self._cachedRounded
+        if cached is not None and cached[1] == self._identity(queries, keys, values):
+            # the forward's tf32-rounded copies of these very tensors
+            q_ptr, k_ptr, v_ptr = _lib.rounded_copies(cached[0], B, self.numHeads, T, self.headDim)
+            dt = _lib.CTFA_DTYPE_TF32
         ws_bytes = lib.ctfa_backward_workspace_bytes(B, self.numHeads, T, self.headDim, dt)
         ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=queries.device)
         with torch.cuda.device(queries.device):
             status = lib.ctfa_backward(
-                _ptr(queries), _ptr(keys), _ptr(values), _ptr(output), _ptr(outputGrad), _ptr(lse),
+                q_ptr, k_ptr, v_ptr, _ptr(output), _ptr(outputGrad), _ptr(lse),
                 _ptr(dq), _ptr(dk), _ptr(dv), _ptr(ws), ws.numel(),
                 B, self.numHeads, T, self.headDim, dt, int(self.causal), _stream_handle(queries.device),
             )
@@ -147,3 +164,4 @@ class FlashAttentionLayer:
         self.cachedDenominators = None
         self.cachedOutput = None
         self.cachedLSE = None
+        self._cachedRounded = None

@@ -41,6 +41,9 @@ extern "C" {
 #define CTFA_DTYPE_BF16 1 /* bf16 I/O, tcgen05 kind::f16, fp32 softmax/accumulation */
 #define CTFA_DTYPE_F16 2  /* fp16 I/O, tcgen05 kind::f16, fp32 softmax/accumulation */
 #define CTFA_DTYPE_F64 3  /* fp64 I/O, SIMT fp64 kernels */
+#define CTFA_DTYPE_TF32 4 /* fp32 storage whose values are already rounded to tf32 (for example the
+                           * copies ctfa_forward leaves in its workspace): the fp32 tensor-core path
+                           * without the rounding pass over q, k, v */
 
 /* Library version: major*10000 + minor*100 + patch. */
 int ctfa_version(void);
@@ -69,7 +72,11 @@ int ctfa_forward(const void* q, const void* k, const void* v, void* o, float* ls
 /* Bytes of device workspace ctfa_forward needs (0 except for fp32 I/O on the
  * tensor cores, where it holds the round-to-nearest tf32 copies of q, k, v:
  * the MMA itself truncates fp32 operands to tf32, which costs a factor ~4 in
- * accuracy).  workspace may be NULL when this is 0. */
+ * accuracy).  workspace may be NULL when this is 0.  After an fp32 forward
+ * the workspace holds the rounded q, k, v at byte offsets 0, a and 2a, with
+ * a = B*H*T*D*4 rounded up to a multiple of 256; a caller that keeps it may
+ * pass those copies to ctfa_backward as q, k, v with CTFA_DTYPE_TF32, which
+ * skips rounding them again. */
 size_t ctfa_forward_workspace_bytes(int B, int H, int T, int D, int dtype);
 
 /* Bytes of device workspace ctfa_backward needs for this problem. */

@@ -149,3 +149,28 @@ def test_layer_cache_semantics(cuda_device):
     g_recomputed = layer.computeBackward(q, k, v, do)
     for a, b in zip(g_cached, g_recomputed):
         assert torch.equal(a, b)
+
+
+def test_fp32_backward_reuses_forward_rounding(cuda_device, ctfa):
+    """The layer hands the forward's tf32-rounded q/k/v to the backward as
+    CTFA_DTYPE_TF32; results are bitwise those of a plain fp32 backward."""
+    from cudatransformer_b200 import FlashAttentionLayer, _lib
+
+    q, k, v, do = (torch.randn(2, 3, 200, 64, device=cuda_device) for _ in range(4))
+    layer = FlashAttentionLayer(64, 3, causal=True)
+    layer.computeAttention(q, k, v, saveStates=True)
+    assert layer._cachedRounded is not None
+    reused = layer.computeBackward(q, k, v, do)
+    o, lse = layer.cachedOutput, layer.cachedLSE
+    B, H, T, D = q.shape
+    ws = torch.empty(ctfa.ctfa_backward_workspace_bytes(B, H, T, D, _lib.CTFA_DTYPE_F32), dtype=torch.uint8,
+                     device=cuda_device)
+    plain = [torch.empty_like(q) for _ in range(3)]
+    _lib.check(ctfa.ctfa_backward(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(),
+                                  lse.data_ptr(), *(t.data_ptr() for t in plain), ws.data_ptr(), ws.numel(),
+                                  B, H, T, D, _lib.CTFA_DTYPE_F32, 1, torch.cuda.current_stream().cuda_stream),
+               "ctfa_backward")
+    for a, b in zip(reused, plain):
+        assert torch.equal(a, b)
+    q.add_(0)  # bumps the version counter: the cache no longer matches
+    layer.computeBackward(q, k, v, do)
