@@ -61,6 +61,7 @@ struct BwdParams {
   void* dq;          // [BH][q_rows_alloc][HD]
   void* dk;          // [BH][k_rows_alloc][HD]
   void* dv;
+  int accumulate;    // 0: write dq/dk/dv in the I/O type; 1: add into fp32 dq/dk/dv buffers
   unsigned long long wait_limit_ns;
 };
 
@@ -216,6 +217,30 @@ __device__ __forceinline__ void tmem_store_operand(uint32_t taddr, const float (
         regs[i] = std::is_same<DT, __nv_bfloat16>::value ? pack_bf16x2(v[N - 32 + 2 * i], v[N - 32 + 2 * i + 1])
                                                          : pack_f16x2(v[N - 32 + 2 * i], v[N - 32 + 2 * i + 1]);
       tmem_st16(taddr + (N / 64) * 32, regs);
+    }
+  }
+}
+
+// Add `COLS` fp32 TMEM columns of this thread's lane into a row of an fp32
+// buffer (the block entry points accumulate over ring steps; each CTA owns its
+// rows within one launch, so no atomics).
+template <int COLS>
+__device__ __forceinline__ void tmem_row_accumulate(uint32_t taddr, float* dst, bool store) {
+#pragma unroll
+  for (int c = 0; c < COLS / 32; ++c) {
+    uint32_t regs[32];
+    tmem_ld32(taddr + c * 32, regs);
+    tmem_wait_ld();
+    if (!store) continue;
+    float4* d4 = reinterpret_cast<float4*>(dst + c * 32);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float4 a = d4[i];
+      a.x += __uint_as_float(regs[4 * i]);
+      a.y += __uint_as_float(regs[4 * i + 1]);
+      a.z += __uint_as_float(regs[4 * i + 2]);
+      a.w += __uint_as_float(regs[4 * i + 3]);
+      d4[i] = a;
     }
   }
 }
@@ -516,10 +541,19 @@ __global__ void __launch_bounds__(320, 1)
       tc_fence_after();
       const size_t row_index = (size_t)bh * p.k_rows_alloc + p.k_row0 + key;
       const int col = h * (HD / 2);
-      tmem_row_to_global<DT, HD / 2>(tbase + lane_off + C::KV_DK + col,
-                                     reinterpret_cast<DT*>(p.dk) + row_index * HD + col, key_ok, n_it == 0);
-      tmem_row_to_global<DT, HD / 2>(tbase + lane_off + C::KV_DV + col,
-                                     reinterpret_cast<DT*>(p.dv) + row_index * HD + col, key_ok, n_it == 0);
+      if (p.accumulate) {
+        if (n_it > 0) {
+          tmem_row_accumulate<HD / 2>(tbase + lane_off + C::KV_DK + col,
+                                      reinterpret_cast<float*>(p.dk) + row_index * HD + col, key_ok);
+          tmem_row_accumulate<HD / 2>(tbase + lane_off + C::KV_DV + col,
+                                      reinterpret_cast<float*>(p.dv) + row_index * HD + col, key_ok);
+        }
+      } else {
+        tmem_row_to_global<DT, HD / 2>(tbase + lane_off + C::KV_DK + col,
+                                       reinterpret_cast<DT*>(p.dk) + row_index * HD + col, key_ok, n_it == 0);
+        tmem_row_to_global<DT, HD / 2>(tbase + lane_off + C::KV_DV + col,
+                                       reinterpret_cast<DT*>(p.dv) + row_index * HD + col, key_ok, n_it == 0);
+      }
     }
   }
 
@@ -763,8 +797,14 @@ __global__ void __launch_bounds__(320, 1)
     if (ok) {
       tc_fence_after();
       const int col = h * (HD / 2);
-      tmem_row_to_global<DT, HD / 2>(tbase + lane_off + C::Q_DQ + col,
-                                     reinterpret_cast<DT*>(p.dq) + lrow * HD + col, q_ok, n_kv == 0);
+      if (p.accumulate) {
+        if (n_kv > 0)
+          tmem_row_accumulate<HD / 2>(tbase + lane_off + C::Q_DQ + col,
+                                      reinterpret_cast<float*>(p.dq) + lrow * HD + col, q_ok);
+      } else {
+        tmem_row_to_global<DT, HD / 2>(tbase + lane_off + C::Q_DQ + col,
+                                       reinterpret_cast<DT*>(p.dq) + lrow * HD + col, q_ok, n_kv == 0);
+      }
     }
   }
 

@@ -47,6 +47,7 @@ struct FwdParams {
   int n_groups;        // CTA groups of NQ query tiles per head
   float scale_log2;    // softmax scale * log2(e)
   void* o;             // [BH][q_rows_alloc][HD] DT
+  float* o_f32;        // when set: fp32 output rows here instead of o (block partials)
   float* lse;          // [BH][q_rows_alloc] natural-log logsumexp (nullable)
   unsigned long long wait_limit_ns;
 };
@@ -408,12 +409,19 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
       const bool row_ok = q_local < p.Tq;
       const size_t row_index = (size_t)bh * p.q_rows_alloc + p.q_row0 + q_local;
       DT* orow = reinterpret_cast<DT*>(p.o) + row_index * HD;
+      float* orow32 = p.o_f32 != nullptr ? p.o_f32 + row_index * HD : nullptr;
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t regs[32];
         tmem_ld32(o_addr + c * 32, regs);
         tmem_wait_ld();
-        if (row_ok) {
+        if (row_ok && orow32 != nullptr) {
+          float4* dst = reinterpret_cast<float4*>(orow32 + c * 32);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            dst[i] = make_float4(__uint_as_float(regs[4 * i]) * inv_l, __uint_as_float(regs[4 * i + 1]) * inv_l,
+                                 __uint_as_float(regs[4 * i + 2]) * inv_l, __uint_as_float(regs[4 * i + 3]) * inv_l);
+        } else if (row_ok) {
           if constexpr (C::EB == 4) {
             float4* dst = reinterpret_cast<float4*>(orow + c * 32);
 #pragma unroll

@@ -108,6 +108,8 @@ struct Problem {
   int q_rows, k_rows;  // rows per head in the allocations
   int q_row0, k_row0;
   int causal, causal_offset;
+  float* o_f32 = nullptr;  // forward: fp32 output rows instead of o (block partials)
+  int accumulate = 0;      // backward: add into fp32 dq/dk/dv instead of writing the I/O type
 };
 
 bool tensor_core_shape(const Problem& pr) {
@@ -138,6 +140,7 @@ int launch_fwd_tc(const Problem& pr, const void* q, const void* k, const void* v
   p.n_groups = (q_tiles + NQ - 1) / NQ;
   p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)HD));
   p.o = o;
+  p.o_f32 = pr.o_f32;
   p.lse = lse;
   p.wait_limit_ns = g_wait_limit_ns;
   auto kern = attn_fwd_sm100<DT, HD, NQ, BN, ST>;
@@ -414,6 +417,7 @@ int launch_bwd_tc(const Problem& pr, const void* q, const void* k, const void* v
   p.dq = dq;
   p.dk = dk;
   p.dv = dv;
+  p.accumulate = pr.accumulate;
   p.wait_limit_ns = g_wait_limit_ns;
   const int n_kt = (pr.Tk + C::KV_KEYS - 1) / C::KV_KEYS;
   const int n_qt = (pr.Tq + C::Q_ROWS - 1) / C::Q_ROWS;
@@ -633,6 +637,139 @@ extern "C" int ctfa_backward_noalloc(const void* q, const void* k, const void* v
   void* ws = nullptr;
   if ((s = noalloc_scratch(&ws)) != CTFA_OK) return s;
   return backward_impl(pr, q, k, v, o, dO, lse, dq, dk, dv, ws, (cudaStream_t)stream);
+}
+
+// ---------------------------------------------------------------------------
+// Block entry points for sequence-parallel (ring) attention.
+// ---------------------------------------------------------------------------
+namespace {
+
+__global__ void __launch_bounds__(256)
+    merge_blocks_kernel(float* o_acc, float* lse_acc, const float* o_blk, const float* lse_blk, int BH, int rows,
+                        int row0, int T, int D, int init) {
+  const long long w = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= (long long)BH * T) return;
+  const long long bh = w / T, i = w % T;
+  const size_t r = (size_t)bh * rows + row0 + i;
+  float* oa = o_acc + r * D;
+  const float* ob = o_blk + r * D;
+  if (init) {
+    for (int d = lane; d < D; d += 32) oa[d] = ob[d];
+    if (lane == 0) lse_acc[r] = lse_blk[r];
+    return;
+  }
+  const float l1 = lse_acc[r], l2 = lse_blk[r];
+  const float mx = fmaxf(l1, l2);
+  if (mx == -INFINITY) return;
+  const float w1 = __expf(l1 - mx), w2 = __expf(l2 - mx);
+  const float inv = 1.f / (w1 + w2);
+  for (int d = lane; d < D; d += 32) oa[d] = (oa[d] * w1 + ob[d] * w2) * inv;
+  __syncwarp();
+  if (lane == 0) lse_acc[r] = mx + __logf(w1 + w2);
+}
+
+template <typename DT>
+__global__ void __launch_bounds__(256) convert_f32_kernel(const float* src, DT* dst, size_t n) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    dst[i] = from_acc<DT>(src[i]);
+}
+
+int check_block(const void* q, const void* k, const void* v, int B, int H, int D, int dtype, int q_rows,
+                int q_row0, int Tq, int k_rows, int k_row0, int Tk) {
+  int s = check_common(B, H, Tq > 0 ? Tq : 1, D, dtype);
+  if (s != CTFA_OK) return s;
+  if (!q || !k || !v) return fail(CTFA_ERR_INVALID_ARGUMENT, "q, k and v must be non-null");
+  if (dtype != CTFA_DTYPE_BF16 && dtype != CTFA_DTYPE_F16)
+    return fail(CTFA_ERR_UNSUPPORTED, "block entry points take bf16 or fp16 I/O");
+  if (D != 64 && D != 128) return fail(CTFA_ERR_UNSUPPORTED, "block entry points take head dim 64 or 128");
+  if (Tq <= 0 || Tk <= 0 || q_row0 < 0 || k_row0 < 0 || q_row0 + Tq > q_rows || k_row0 + Tk > k_rows)
+    return fail(CTFA_ERR_INVALID_ARGUMENT, "row range outside the allocation");
+  return CTFA_OK;
+}
+
+Problem block_problem(int B, int H, int D, int dtype, int q_rows, int q_row0, int Tq, int k_rows, int k_row0,
+                      int Tk, int causal, int causal_offset) {
+  Problem pr;
+  pr.B = B;
+  pr.H = H;
+  pr.D = D;
+  pr.dtype = dtype;
+  pr.Tq = Tq;
+  pr.Tk = Tk;
+  pr.q_rows = q_rows;
+  pr.k_rows = k_rows;
+  pr.q_row0 = q_row0;
+  pr.k_row0 = k_row0;
+  pr.causal = causal ? 1 : 0;
+  pr.causal_offset = causal_offset;
+  return pr;
+}
+
+}  // namespace
+
+extern "C" int ctfa_forward_block(const void* q, const void* k, const void* v, float* o_blk, float* lse_blk, int B,
+                                  int H, int D, int dtype, int q_rows, int q_row0, int Tq, int k_rows, int k_row0,
+                                  int Tk, int causal, int causal_offset, void* stream) {
+  int s = check_block(q, k, v, B, H, D, dtype, q_rows, q_row0, Tq, k_rows, k_row0, Tk);
+  if (s != CTFA_OK) return s;
+  if (!o_blk || !lse_blk) return fail(CTFA_ERR_INVALID_ARGUMENT, "o_blk and lse_blk must be non-null");
+  Problem pr = block_problem(B, H, D, dtype, q_rows, q_row0, Tq, k_rows, k_row0, Tk, causal, causal_offset);
+  pr.o_f32 = o_blk;
+  return forward_impl(pr, q, k, v, o_blk, lse_blk, nullptr, (cudaStream_t)stream);
+}
+
+extern "C" int ctfa_merge_blocks(float* o_acc, float* lse_acc, const float* o_blk, const float* lse_blk, int B,
+                                 int H, int D, int rows, int row0, int T, int init, void* stream) {
+  if (!o_acc || !lse_acc || !o_blk || !lse_blk) return fail(CTFA_ERR_INVALID_ARGUMENT, "null pointer");
+  if (B <= 0 || H <= 0 || D <= 0 || T <= 0 || row0 < 0 || row0 + T > rows)
+    return fail(CTFA_ERR_INVALID_ARGUMENT, "bad sizes");
+  const long long warps = (long long)B * H * T;
+  merge_blocks_kernel<<<warps_grid(warps), 256, 0, (cudaStream_t)stream>>>(o_acc, lse_acc, o_blk, lse_blk, B * H,
+                                                                           rows, row0, T, D, init);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? CTFA_OK : cuda_fail(e, "launch merge_blocks_kernel");
+}
+
+extern "C" int ctfa_convert_f32(const float* src, void* dst, int dtype, size_t n, void* stream) {
+  if (!src || !dst) return fail(CTFA_ERR_INVALID_ARGUMENT, "null pointer");
+  const unsigned grid = (unsigned)std::min<size_t>((n + 255) / 256, 148 * 16);
+  if (n == 0) return CTFA_OK;
+  if (dtype == CTFA_DTYPE_BF16)
+    convert_f32_kernel<__nv_bfloat16><<<grid, 256, 0, (cudaStream_t)stream>>>(src, (__nv_bfloat16*)dst, n);
+  else if (dtype == CTFA_DTYPE_F16)
+    convert_f32_kernel<__half><<<grid, 256, 0, (cudaStream_t)stream>>>(src, (__half*)dst, n);
+  else if (dtype == CTFA_DTYPE_F32)
+    convert_f32_kernel<float><<<grid, 256, 0, (cudaStream_t)stream>>>(src, (float*)dst, n);
+  else
+    return fail(CTFA_ERR_UNSUPPORTED, "convert to fp32, bf16 or fp16 only");
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? CTFA_OK : cuda_fail(e, "launch convert_f32_kernel");
+}
+
+extern "C" size_t ctfa_backward_block_workspace_bytes(int B, int H, int Tq, int D, int dtype) {
+  if (check_common(B, H, Tq, D, dtype) != CTFA_OK) return 0;
+  Problem pr = block_problem(B, H, D, dtype, Tq, 0, Tq, Tq, 0, Tq, 0, 0);
+  return 2 * align256(padded_rows(pr) * sizeof(float));
+}
+
+extern "C" int ctfa_backward_block(const void* q, const void* k, const void* v, const void* o, const void* dO,
+                                   const float* lse, float* dq_acc, float* dk_acc, float* dv_acc, void* workspace,
+                                   size_t workspace_bytes, int B, int H, int D, int dtype, int q_rows, int q_row0,
+                                   int Tq, int k_rows, int k_row0, int Tk, int causal, int causal_offset,
+                                   void* stream) {
+  int s = check_block(q, k, v, B, H, D, dtype, q_rows, q_row0, Tq, k_rows, k_row0, Tk);
+  if (s != CTFA_OK) return s;
+  if (!o || !dO || !lse || !dq_acc || !dk_acc || !dv_acc)
+    return fail(CTFA_ERR_INVALID_ARGUMENT, "o, dO, lse, dq_acc, dk_acc and dv_acc must be non-null");
+  Problem pr = block_problem(B, H, D, dtype, q_rows, q_row0, Tq, k_rows, k_row0, Tk, causal, causal_offset);
+  pr.accumulate = 1;
+  const size_t need = ctfa_backward_block_workspace_bytes(B, H, Tq, D, dtype);
+  if (!workspace || workspace_bytes < need)
+    return fail(CTFA_ERR_WORKSPACE, "workspace needs " + std::to_string(need) + " bytes");
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return fail(CTFA_ERR_MISALIGNED, "workspace must be 256-byte aligned");
+  return backward_impl(pr, q, k, v, o, dO, lse, dq_acc, dk_acc, dv_acc, workspace, (cudaStream_t)stream);
 }
 
 extern "C" int ctfa_check_device_error(void* stream) {

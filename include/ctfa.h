@@ -133,6 +133,44 @@ int ctfa_backward_noalloc(const void* q, const void* k, const void* v, const voi
                           int causal, void* stream);
 
 /*
+ * Block entry points for sequence-parallel (ring) attention.  No counterpart
+ * in the reference, which runs one device and one sequence (its kernel loops
+ * over all keys, flash_attention.cu:97).  They run the same tensor-core
+ * kernels on row ranges of each head (bf16 / fp16 I/O, head dim 64 or 128):
+ * query rows [q_row0, q_row0+Tq) of an allocation [B, H, q_rows, D] against
+ * key/value rows [k_row0, k_row0+Tk) of an allocation [B, H, k_rows, D].
+ * causal = 1: key j (local to the block) is visible to query i (local) iff
+ * j <= i + causal_offset; causal = 0: every key is visible.
+ */
+
+/* Partial attention of one block: normalised output rows (fp32) into o_blk
+ * ([B, H, q_rows, D], same rows as q) and their logsumexp into lse_blk
+ * ([B, H, q_rows]). */
+int ctfa_forward_block(const void* q, const void* k, const void* v, float* o_blk, float* lse_blk, int B, int H,
+                       int D, int dtype, int q_rows, int q_row0, int Tq, int k_rows, int k_row0, int Tk,
+                       int causal, int causal_offset, void* stream);
+
+/* Fold one block's partial (o_blk, lse_blk) into the running (o_acc, lse_acc)
+ * on rows [row0, row0+T) of [B, H, rows, *] fp32 buffers: logsumexp-weighted
+ * average.  init = 1 copies instead (first block of those rows). */
+int ctfa_merge_blocks(float* o_acc, float* lse_acc, const float* o_blk, const float* lse_blk, int B, int H, int D,
+                      int rows, int row0, int T, int init, void* stream);
+
+/* n fp32 values to CTFA_DTYPE_BF16 / F16 / F32 (round to nearest). */
+int ctfa_convert_f32(const float* src, void* dst, int dtype, size_t n, void* stream);
+
+/* Workspace of ctfa_backward_block for Tq query rows. */
+size_t ctfa_backward_block_workspace_bytes(int B, int H, int Tq, int D, int dtype);
+
+/* Gradient contributions of one block, added into fp32 buffers: dq_acc rows
+ * like q, dk_acc / dv_acc rows like k.  o, dO: the final forward output and
+ * its gradient (rows like q); lse: the final logsumexp ([B, H, q_rows]). */
+int ctfa_backward_block(const void* q, const void* k, const void* v, const void* o, const void* dO,
+                        const float* lse, float* dq_acc, float* dk_acc, float* dv_acc, void* workspace,
+                        size_t workspace_bytes, int B, int H, int D, int dtype, int q_rows, int q_row0, int Tq,
+                        int k_rows, int k_row0, int Tk, int causal, int causal_offset, void* stream);
+
+/*
  * Bound, in nanoseconds, on every wait inside the kernels (default 2e9).  A
  * kernel that waits longer records CTFA_ERR_DEVICE_TIMEOUT in a device error
  * word and exits without touching its outputs further.
