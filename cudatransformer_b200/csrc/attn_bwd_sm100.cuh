@@ -75,52 +75,96 @@ __device__ __forceinline__ float load_as_float(const DT* p) {
     return __half2float(*p);
 }
 
-// One warp per query row: delta = rowsum(O * dO) in fp32.  For fp32 I/O it
-// also writes the tf32-rounded dO that the MMAs read, and forms delta from
-// that same rounded dO, so that sum_j P_ij dP_ij == delta_i holds for the
-// values the tensor cores see (dS then cancels exactly where it should).
+// delta = rowsum(O * dO) in fp32, a group of 2-8 threads per query row, each
+// thread loading four 16-byte vectors of O and of dO (enough bytes in flight
+// per SM to keep HBM busy).  For fp32 I/O it also writes the tf32-rounded dO
+// that the MMAs read, and forms delta from that same rounded dO, so that
+// sum_j P_ij dP_ij == delta_i holds for the values the tensor cores see (dS
+// then cancels exactly where it should).
 template <typename DT, int HD>
-__global__ void __launch_bounds__(256) attn_bwd_prep(BwdPrepParams p) {
-  const long long w = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (w >= p.rows) return;
-  const long long bh = w / p.Tq_pad, i = w % p.Tq_pad;
-  if (i >= p.Tq) {  // padding row of the last tile
-    if (lane == 0) {
-      p.delta[w] = 0.f;
-      p.lse2[w] = INFINITY;
-    }
-    return;
-  }
-  const size_t row = ((size_t)bh * p.q_rows_alloc + p.q_row0 + i) * HD;
-  const DT* o = reinterpret_cast<const DT*>(p.o) + row;
-  const DT* g = reinterpret_cast<const DT*>(p.dO) + row;
-  float s = 0.f;
+struct PrepShape {
+  static constexpr int VEC = 16 / (int)sizeof(DT);  // elements per 16-byte vector
+  static constexpr int NV = HD / VEC;               // vectors per row
+  static constexpr int VPT = 4;                     // vectors per thread
+  static constexpr int TPR = NV / VPT;              // threads per row
+  static_assert(TPR >= 1 && TPR <= 32 && (32 % TPR) == 0, "row group must tile a warp");
+};
+
+template <typename DT>
+__device__ __forceinline__ void vec_to_float(const uint4& u, float* f) {
   if constexpr (sizeof(DT) == 4) {
-    if (p.dO_round != nullptr) {
-      float* gr = p.dO_round + row;
-#pragma unroll
-      for (int d = lane; d < HD; d += 32) {
-        const float r = __uint_as_float(f32_to_tf32_rna(load_as_float(g + d)));
-        gr[d] = r;
-        s += load_as_float(o + d) * r;
-      }
-    } else {
-#pragma unroll
-      for (int d = lane; d < HD; d += 32) s += load_as_float(o + d) * load_as_float(g + d);
-    }
+    f[0] = __uint_as_float(u.x);
+    f[1] = __uint_as_float(u.y);
+    f[2] = __uint_as_float(u.z);
+    f[3] = __uint_as_float(u.w);
   } else {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-    for (int d = lane; d < HD; d += 32) s += load_as_float(o + d) * load_as_float(g + d);
-  }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-  if (lane == 0) {
-    p.delta[w] = s;
-    p.lse2[w] = p.lse[bh * p.q_rows_alloc + p.q_row0 + i] * 1.4426950408889634f;
+    for (int i = 0; i < 4; ++i) {
+      if constexpr (std::is_same<DT, __nv_bfloat16>::value) {
+        f[2 * i] = __uint_as_float(w[i] << 16);
+        f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+      } else {
+        const __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+        const float2 x = __half22float2(h);
+        f[2 * i] = x.x;
+        f[2 * i + 1] = x.y;
+      }
+    }
   }
 }
 
+template <typename DT, int HD>
+__global__ void __launch_bounds__(256) attn_bwd_prep(BwdPrepParams p) {
+  using S = PrepShape<DT, HD>;
+  constexpr int VEC = S::VEC, TPR = S::TPR, VPT = S::VPT;
+  const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long w = t / TPR;  // padded query row
+  const int sub = (int)(t % TPR);
+  // whole row groups share a warp; every lane reaches the shuffles below
+  const bool in = w < p.rows;
+  const long long bh = in ? w / p.Tq_pad : 0, i = in ? w % p.Tq_pad : 0;
+  const bool real = in && i < p.Tq;
+  float s = 0.f;
+  if (real) {
+    const size_t row = ((size_t)bh * p.q_rows_alloc + p.q_row0 + i) * HD;
+    const uint4* o4 = reinterpret_cast<const uint4*>(reinterpret_cast<const DT*>(p.o) + row);
+    const uint4* g4 = reinterpret_cast<const uint4*>(reinterpret_cast<const DT*>(p.dO) + row);
+    uint4 ov[VPT], gv[VPT];
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      ov[v] = __ldcs(o4 + sub + v * TPR);
+      gv[v] = __ldcs(g4 + sub + v * TPR);
+    }
+    float* gr = p.dO_round != nullptr ? p.dO_round + row : nullptr;
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      float of[VEC], gf[VEC];
+      vec_to_float<DT>(ov[v], of);
+      vec_to_float<DT>(gv[v], gf);
+      if constexpr (sizeof(DT) == 4) {
+        if (gr != nullptr) {
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) gf[e] = __uint_as_float(f32_to_tf32_rna(gf[e]));
+          reinterpret_cast<float4*>(gr)[sub + v * TPR] = make_float4(gf[0], gf[1], gf[2], gf[3]);
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) s = fmaf(of[e], gf[e], s);
+    }
+  }
+#pragma unroll
+  for (int off = TPR / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (in && sub == 0) {
+    if (real) {
+      p.delta[w] = s;
+      p.lse2[w] = p.lse[bh * p.q_rows_alloc + p.q_row0 + i] * 1.4426950408889634f;
+    } else {  // padding row of the last tile
+      p.delta[w] = 0.f;
+      p.lse2[w] = INFINITY;
+    }
+  }
+}
 
 template <typename DT, int HD>
 struct BwdConfig {

@@ -10,7 +10,10 @@
 //   CTA  = NQ query tiles of 128 rows of one (batch, head), sharing K/V tiles.
 //   warps 0..4*NQ-1 : softmax, one warpgroup per query tile, one thread per
 //                     query row (= TMEM lane).
-//   warp  4*NQ      : TMA producer (Q once, then K/V tiles through ST stages).
+//   warp  4*NQ      : TMA producer (Q once, then K tiles through KST stages and
+//                     V tiles through VST stages, K one tile ahead of V: the
+//                     S GEMM of tile j+1 needs K well before P V of tile j+1
+//                     needs V).
 //   warp  4*NQ+1    : tcgen05.mma issuer (one elected lane).
 //   warps 4*NQ+2,3  : spare (they complete the producer warpgroup, which hands
 //                     its registers to the softmax warpgroups via setmaxnreg).
@@ -52,7 +55,7 @@ struct FwdParams {
   unsigned long long wait_limit_ns;
 };
 
-template <typename DT, int HD, int NQ, int BN, int ST>
+template <typename DT, int HD, int NQ, int BN, int KST, int VST>
 struct FwdConfig {
   static constexpr int BM = 128;
   static constexpr int EB = (int)sizeof(DT);
@@ -65,8 +68,8 @@ struct FwdConfig {
   static constexpr int KSTEP_PV = BN / K_PER_PV;
   static constexpr int P_COLS = (EB == 4) ? BN : BN / 2;
   static constexpr uint32_t TMEM_COLS = tmem_cols_for(NQ * (BN + HD));
-  static constexpr int NUM_BARS = 1 + 4 * ST + 3 * NQ + 1;
-  static constexpr int SMEM_BYTES = 1024 + NQ * Q_TILE_BYTES + 2 * ST * KV_TILE_BYTES + NUM_BARS * 8 + 16;
+  static constexpr int NUM_BARS = 1 + 2 * KST + 2 * VST + 3 * NQ + 1;
+  static constexpr int SMEM_BYTES = 1024 + NQ * Q_TILE_BYTES + (KST + VST) * KV_TILE_BYTES + NUM_BARS * 8 + 16;
   // NQ softmax warpgroups + one producer warpgroup (TMA warp, MMA warp, two
   // spare warps) so that registers can be rebalanced per warpgroup.
   static constexpr int THREADS = NQ * 128 + 128;
@@ -79,13 +82,14 @@ struct FwdConfig {
   static_assert(HD * EB % 128 == 0, "head dim must fill whole 128-byte rows");
   static_assert(BN % 32 == 0 && BN <= 256, "key tile");
   static_assert(NQ * (BN + HD) <= 512, "TMEM budget");
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
 
-template <typename DT, int HD, int NQ, int BN, int ST>
+template <typename DT, int HD, int NQ, int BN, int KST, int VST>
 __global__ void __launch_bounds__(NQ * 128 + 128, 1)
     attn_fwd_sm100(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
-  using C = FwdConfig<DT, HD, NQ, BN, ST>;
+  using C = FwdConfig<DT, HD, NQ, BN, KST, VST>;
   constexpr int BM = C::BM;
   constexpr int kKind = DTypeTraits<DT>::kKind;
   constexpr uint32_t kFmt = DTypeTraits<DT>::kFmt;
@@ -96,14 +100,14 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
   uint8_t* sK = sQ + NQ * C::Q_TILE_BYTES;
-  uint8_t* sV = sK + ST * C::KV_TILE_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + ST * C::KV_TILE_BYTES);
+  uint8_t* sV = sK + KST * C::KV_TILE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + VST * C::KV_TILE_BYTES);
   uint64_t* q_full = bars;
   uint64_t* k_full = q_full + 1;
-  uint64_t* k_empty = k_full + ST;
-  uint64_t* v_full = k_empty + ST;
-  uint64_t* v_empty = v_full + ST;
-  uint64_t* s_full = v_empty + ST;
+  uint64_t* k_empty = k_full + KST;
+  uint64_t* v_full = k_empty + KST;
+  uint64_t* v_empty = v_full + VST;
+  uint64_t* s_full = v_empty + VST;
   uint64_t* p_full = s_full + NQ;
   uint64_t* o_full = p_full + NQ;
   uint64_t* done_bar = o_full + NQ;
@@ -142,9 +146,11 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < ST; ++s) {
+    for (int s = 0; s < KST; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < VST; ++s) {
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
@@ -188,32 +194,39 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
           tma_load_3d(sQ + k * C::Q_TILE_BYTES + b * BM * 128, &tm_q, q_full, b * C::E128, row, bh);
       }
       int issued_k = 0, issued_v = 0;
-      for (int j = 0; j < n_max; ++j) {
-        const int st = j % ST;
-        const uint32_t ph = (j / ST) & 1;
-        const int row = p.k_row0 + j * BN;
-        if (!mbar_wait(&k_empty[st], ph ^ 1, abort_flag, limit, 1)) break;
-        mbar_arrive_expect_tx(&k_full[st], C::KV_TILE_BYTES);
+      // slot t loads K_t and V_{t-1}: K runs one tile ahead of V
+      for (int t = 0; t <= n_max; ++t) {
+        if (t < n_max) {
+          const int st = t % KST;
+          if (!mbar_wait(&k_empty[st], ((t / KST) & 1) ^ 1, abort_flag, limit, 1)) break;
+          mbar_arrive_expect_tx(&k_full[st], C::KV_TILE_BYTES);
 #pragma unroll
-        for (int b = 0; b < C::KBLK; ++b)
-          tma_load_3d(sK + st * C::KV_TILE_BYTES + b * BN * 128, &tm_k, &k_full[st], b * C::E128, row, bh);
-        issued_k = j + 1;
-        if (!mbar_wait(&v_empty[st], ph ^ 1, abort_flag, limit, 2)) break;
-        mbar_arrive_expect_tx(&v_full[st], C::KV_TILE_BYTES);
+          for (int b = 0; b < C::KBLK; ++b)
+            tma_load_3d(sK + st * C::KV_TILE_BYTES + b * BN * 128, &tm_k, &k_full[st], b * C::E128,
+                        p.k_row0 + t * BN, bh);
+          issued_k = t + 1;
+        }
+        if (t >= 1) {
+          const int j = t - 1;
+          const int st = j % VST;
+          if (!mbar_wait(&v_empty[st], ((j / VST) & 1) ^ 1, abort_flag, limit, 2)) break;
+          mbar_arrive_expect_tx(&v_full[st], C::KV_TILE_BYTES);
 #pragma unroll
-        for (int b = 0; b < C::KBLK; ++b)
-          tma_load_3d(sV + st * C::KV_TILE_BYTES + b * BN * 128, &tm_v, &v_full[st], b * C::E128, row, bh);
-        issued_v = j + 1;
+          for (int b = 0; b < C::KBLK; ++b)
+            tma_load_3d(sV + st * C::KV_TILE_BYTES + b * BN * 128, &tm_v, &v_full[st], b * C::E128,
+                        p.k_row0 + j * BN, bh);
+          issued_v = j + 1;
+        }
       }
       // On an aborted run some loads may still be landing: wait (bounded,
       // ignoring the abort flag) for the last load issued into each stage.
       if (*abort_flag) {
         const uint64_t t0 = globaltimer_ns();
-        for (int j = max(0, issued_k - ST); j < issued_k; ++j)
-          while (!mbar_try_wait(&k_full[j % ST], (j / ST) & 1) && globaltimer_ns() - t0 < limit) {
+        for (int j = max(0, issued_k - KST); j < issued_k; ++j)
+          while (!mbar_try_wait(&k_full[j % KST], (j / KST) & 1) && globaltimer_ns() - t0 < limit) {
           }
-        for (int j = max(0, issued_v - ST); j < issued_v; ++j)
-          while (!mbar_try_wait(&v_full[j % ST], (j / ST) & 1) && globaltimer_ns() - t0 < limit) {
+        for (int j = max(0, issued_v - VST); j < issued_v; ++j)
+          while (!mbar_try_wait(&v_full[j % VST], (j / VST) & 1) && globaltimer_ns() - t0 < limit) {
           }
         while (!mbar_try_wait(q_full, 0) && globaltimer_ns() - t0 < limit) {
         }
@@ -261,9 +274,9 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
         umma_commit(&k_empty[0]);
       }
       for (int j = 0; ok && j < n_max; ++j) {
-        const int st = j % ST;
-        const int st1 = (j + 1) % ST;
-        if (!(ok = mbar_wait(&v_full[st], (j / ST) & 1, abort_flag, limit, 5))) break;
+        const int st = j % VST;
+        const int st1 = (j + 1) % KST;
+        if (!(ok = mbar_wait(&v_full[st], (j / VST) & 1, abort_flag, limit, 5))) break;
         bool next_k = false;
 #pragma unroll
         for (int k = 0; k < NQ; ++k) {
@@ -274,7 +287,7 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
           if (j == n_kv[k] - 1) umma_commit(&o_full[k]);
           if (j + 1 < n_kv[k]) {
             if (!next_k) {
-              if (!(ok = mbar_wait(&k_full[st1], ((j + 1) / ST) & 1, abort_flag, limit, 7))) break;
+              if (!(ok = mbar_wait(&k_full[st1], ((j + 1) / KST) & 1, abort_flag, limit, 7))) break;
               tc_fence_after();
               next_k = true;
             }

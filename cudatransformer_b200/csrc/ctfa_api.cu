@@ -118,10 +118,10 @@ bool tensor_core_shape(const Problem& pr) {
          (pr.D == 64 || pr.D == 128);
 }
 
-template <typename DT, int HD, int NQ, int BN, int ST>
+template <typename DT, int HD, int NQ, int BN, int KST, int VST>
 int launch_fwd_tc(const Problem& pr, const void* q, const void* k, const void* v, void* o, float* lse,
                   cudaStream_t stream) {
-  using C = FwdConfig<DT, HD, NQ, BN, ST>;
+  using C = FwdConfig<DT, HD, NQ, BN, KST, VST>;
   CUtensorMap mq, mk, mv;
   int s;
   if ((s = make_map(&mq, q, pr.dtype, HD, pr.q_rows, pr.B * pr.H, 128)) != CTFA_OK) return s;
@@ -143,7 +143,7 @@ int launch_fwd_tc(const Problem& pr, const void* q, const void* k, const void* v
   p.o_f32 = pr.o_f32;
   p.lse = lse;
   p.wait_limit_ns = g_wait_limit_ns;
-  auto kern = attn_fwd_sm100<DT, HD, NQ, BN, ST>;
+  auto kern = attn_fwd_sm100<DT, HD, NQ, BN, KST, VST>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attn_fwd_sm100)");
   const long long grid = (long long)p.n_groups * p.BH;
@@ -188,9 +188,25 @@ __global__ void __launch_bounds__(256) round_tf32_kernel(RoundJob job) {
   const int t = blockIdx.y;
   const float4* in = job.in[t];
   float4* out = job.out[t];
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < job.n4;
-       i += (long long)gridDim.x * blockDim.x) {
-    float4 x = in[i];
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  // four independent 16-byte loads in flight per thread; the inputs are read
+  // once (evict-first), the rounded copies stay in L2 for the kernel after
+  for (; i + 3 * stride < job.n4; i += 4 * stride) {
+    float4 x[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) x[u] = __ldcs(in + i + u * stride);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      x[u].x = __uint_as_float(f32_to_tf32_rna(x[u].x));
+      x[u].y = __uint_as_float(f32_to_tf32_rna(x[u].y));
+      x[u].z = __uint_as_float(f32_to_tf32_rna(x[u].z));
+      x[u].w = __uint_as_float(f32_to_tf32_rna(x[u].w));
+      out[i + u * stride] = x[u];
+    }
+  }
+  for (; i < job.n4; i += stride) {
+    float4 x = __ldcs(in + i);
     x.x = __uint_as_float(f32_to_tf32_rna(x.x));
     x.y = __uint_as_float(f32_to_tf32_rna(x.y));
     x.z = __uint_as_float(f32_to_tf32_rna(x.z));
@@ -210,8 +226,9 @@ int launch_round(const void* const* in, void* const* out, int count, size_t elem
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // one resident wave (8 blocks of 256 threads per SM) over all tensors
   const long long want = (job.n4 + 255) / 256;
-  dim3 grid((unsigned)std::min<long long>(want, (long long)sms * 8), count);
+  dim3 grid((unsigned)std::max<long long>(1, std::min<long long>(want, ((long long)sms * 8 + count - 1) / count)), count);
   round_tf32_kernel<<<grid, 256, 0, stream>>>(job);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? CTFA_OK : cuda_fail(e, "launch round_tf32_kernel");
@@ -252,18 +269,18 @@ int forward_impl(const Problem& pr, const void* q, const void* k, const void* v,
         void* r[3] = {w, w + align256(n * 4), w + 2 * align256(n * 4)};
         const void* in[3] = {q, k, v};
         if ((s = launch_round(in, r, 3, n, stream)) != CTFA_OK) return s;
-        return pr.D == 64 ? launch_fwd_tc<float, 64, 2, 128, 2>(pr, r[0], r[1], r[2], o, lse, stream)
-                          : launch_fwd_tc<float, 128, 1, 64, 2>(pr, r[0], r[1], r[2], o, lse, stream);
+        return pr.D == 64 ? launch_fwd_tc<float, 64, 2, 128, 3, 2>(pr, r[0], r[1], r[2], o, lse, stream)
+                          : launch_fwd_tc<float, 128, 1, 64, 3, 2>(pr, r[0], r[1], r[2], o, lse, stream);
       }
       case CTFA_DTYPE_TF32:
-        return pr.D == 64 ? launch_fwd_tc<float, 64, 2, 128, 2>(pr, q, k, v, o, lse, stream)
-                          : launch_fwd_tc<float, 128, 1, 64, 2>(pr, q, k, v, o, lse, stream);
+        return pr.D == 64 ? launch_fwd_tc<float, 64, 2, 128, 3, 2>(pr, q, k, v, o, lse, stream)
+                          : launch_fwd_tc<float, 128, 1, 64, 3, 2>(pr, q, k, v, o, lse, stream);
       case CTFA_DTYPE_BF16:
-        return pr.D == 64 ? launch_fwd_tc<__nv_bfloat16, 64, 2, 128, 3>(pr, q, k, v, o, lse, stream)
-                          : launch_fwd_tc<__nv_bfloat16, 128, 2, 128, 2>(pr, q, k, v, o, lse, stream);
+        return pr.D == 64 ? launch_fwd_tc<__nv_bfloat16, 64, 2, 128, 4, 3>(pr, q, k, v, o, lse, stream)
+                          : launch_fwd_tc<__nv_bfloat16, 128, 2, 128, 3, 2>(pr, q, k, v, o, lse, stream);
       default:
-        return pr.D == 64 ? launch_fwd_tc<__half, 64, 2, 128, 3>(pr, q, k, v, o, lse, stream)
-                          : launch_fwd_tc<__half, 128, 2, 128, 2>(pr, q, k, v, o, lse, stream);
+        return pr.D == 64 ? launch_fwd_tc<__half, 64, 2, 128, 4, 3>(pr, q, k, v, o, lse, stream)
+                          : launch_fwd_tc<__half, 128, 2, 128, 3, 2>(pr, q, k, v, o, lse, stream);
     }
   }
   switch (pr.dtype) {
@@ -373,7 +390,7 @@ int launch_bwd_tc(const Problem& pr, const void* q, const void* k, const void* v
   pp.delta = delta;
   pp.dO_round = (dO_mma != dO) ? reinterpret_cast<float*>(const_cast<void*>(dO_mma)) : nullptr;
   if (!std::is_same<DT, float>::value) record(ev, 0, stream);
-  attn_bwd_prep<DT, HD><<<warps_grid(pp.rows), 256, 0, stream>>>(pp);
+  attn_bwd_prep<DT, HD><<<(unsigned)((pp.rows * PrepShape<DT, HD>::TPR + 255) / 256), 256, 0, stream>>>(pp);
   record(ev, 1, stream);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch attn_bwd_prep");

@@ -332,11 +332,13 @@ __device__ __forceinline__ float ex2_approx(float x) {
 }
 
 // Round fp32 to the nearest tf32 value (ties away from zero); the tensor core
-// reads only the top 19 bits of each 32-bit operand.
+// reads only the top 19 bits of each 32-bit operand.  Integer form: add half
+// of the dropped 13-bit field to the magnitude bits, then clear the field (a
+// carry into the exponent is the correct rounding).  Two integer-pipe
+// instructions, which keeps the conversion off the pipe the exponentials use.
+// Valid for finite inputs (the kernels never feed it inf or NaN).
 __device__ __forceinline__ uint32_t f32_to_tf32_rna(float x) {
-  uint32_t y;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(y) : "f"(x));
-  return y;
+  return (__float_as_uint(x) + 0x1000u) & 0xFFFFE000u;
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
