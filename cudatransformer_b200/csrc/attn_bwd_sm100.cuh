@@ -191,26 +191,39 @@ struct BwdConfig {
   static constexpr int BUDGET = 216 * 1024;
   static constexpr int KV_ST = (BUDGET - 2 * BIG_TILE) / KV_STAGE_BYTES > 3 ? 3 : (BUDGET - 2 * BIG_TILE) / KV_STAGE_BYTES;
   static constexpr int Q_ST = (BUDGET - 2 * BIG_TILE) / Q_STAGE_BYTES > 3 ? 3 : (BUDGET - 2 * BIG_TILE) / Q_STAGE_BYTES;
-  // dK/dV kernel TMEM map (columns, lanes = keys)
+  // dK/dV kernel TMEM map (columns, lanes = keys).  One buffer holds dP^T,
+  // then dS^T (tf32: in place, P^T in the next KV_QT columns; 16-bit: dS^T|P^T
+  // packed per half).  With KV_DBL the buffer is doubled so that the next dP^T
+  // GEMM is queued before the compute warps release the current one.  Off:
+  // measured 4-5% slower on B200 at both tf32 D=64 and bf16 shapes (the early
+  // dP^T delays the dV/dK GEMMs the compute warps are waiting behind).
   static constexpr int KV_HALF = KV_QT / 2;  // score columns per compute warpgroup
   static constexpr int KV_S = 0;
-  static constexpr int KV_DP = KV_QT;        // dP^T; then dS^T (tf32 in place) or dS^T|P^T packed per half
-  static constexpr int KV_P = TF32 ? 2 * KV_QT : KV_QT + KV_HALF / 2;
-  static constexpr int KV_DK = TF32 ? 3 * KV_QT : 2 * KV_QT;
+  static constexpr int KV_BUF = TF32 ? 2 * KV_QT : KV_QT;
+  static constexpr bool KV_DBL = false;
+  static constexpr int KV_NBUF = KV_DBL ? 2 : 1;
+  static constexpr int KV_DK = KV_QT + KV_NBUF * KV_BUF;
   static constexpr int KV_DV = KV_DK + HD;
   static constexpr uint32_t KV_TMEM = tmem_cols_for(KV_DV + HD);
-  // dQ kernel TMEM map (lanes = queries)
+  __host__ __device__ static constexpr int kv_dp(int b) { return KV_QT + b * KV_BUF; }
+  __host__ __device__ static constexpr int kv_p(int b) { return TF32 ? kv_dp(b) + KV_QT : kv_dp(b) + KV_HALF / 2; }
+  // dQ kernel TMEM map (lanes = queries): S, then a dP buffer (dS after the
+  // compute pass: tf32 in place, 16-bit packed per half), doubled with Q_DBL
+  // (off, for the same measured reason as KV_DBL), then the dQ accumulator.
   static constexpr int Q_HALF = Q_KT / 2;
   static constexpr int Q_S = 0;
-  static constexpr int Q_DP = Q_KT;          // dP; then dS (tf32 in place) or dS packed per half
-  static constexpr int Q_DQ = 2 * Q_KT;
+  static constexpr bool Q_DBL = false;
+  static constexpr int Q_NBUF = Q_DBL ? 2 : 1;
+  static constexpr int Q_DQ = Q_KT + Q_NBUF * Q_KT;
   static constexpr uint32_t Q_TMEM = tmem_cols_for(Q_DQ + HD);
+  __host__ __device__ static constexpr int q_dp(int b) { return Q_KT + b * Q_KT; }
   static constexpr int NUM_BARS = 32;
   static constexpr int KV_SMEM = 1024 + 2 * BIG_TILE + KV_ST * KV_STAGE_BYTES + NUM_BARS * 8 + 16;
   static constexpr int Q_SMEM = 1024 + 2 * BIG_TILE + Q_ST * Q_STAGE_BYTES + NUM_BARS * 8 + 16;
   static constexpr int THREADS = 320;
   static_assert(KV_ST >= 1 && Q_ST >= 1, "shared memory budget");
   static_assert(KV_DV + HD <= 512 && Q_DQ + HD <= 512, "TMEM budget");
+  static_assert(!KV_DBL || KV_QT + 2 * KV_BUF + 2 * HD <= 512, "TMEM budget (double-buffered dP^T)");
   static_assert(HD * EB % 128 == 0, "head dim must fill whole 128-byte rows");
   static_assert(KV_HALF % 32 == 0 && Q_HALF % 32 == 0, "compute halves are whole 32-column TMEM loads");
 
@@ -359,9 +372,9 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* q_empty = q_full + ST;  // [ST]
   uint64_t* s_full = q_empty + ST;
   uint64_t* s_free = s_full + 1;
-  uint64_t* dp_full = s_free + 1;
-  uint64_t* p_full = dp_full + 1;
-  uint64_t* acc_full = p_full + 1;
+  uint64_t* dp_full = s_free + 1;  // [2] per dP buffer
+  uint64_t* p_full = dp_full + 2;  // [2] per dP buffer
+  uint64_t* acc_full = p_full + 2;
   uint64_t* done_bar = acc_full + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
@@ -389,8 +402,10 @@ __global__ void __launch_bounds__(320, 1)
     }
     mbar_init(s_full, 1);
     mbar_init(s_free, 256);
-    mbar_init(dp_full, 1);
-    mbar_init(p_full, 256);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&dp_full[b], 1);
+      mbar_init(&p_full[b], 256);
+    }
     mbar_init(acc_full, 1);
     mbar_init(done_bar, 1);
     *abort_flag = 0;
@@ -446,7 +461,8 @@ __global__ void __launch_bounds__(320, 1)
     }
     __syncwarp();
   } else if (warp == MMA_WARP) {
-    if (lane == 0 && n_it > 0) {
+    // The whole warp runs this loop; one elected lane issues each MMA group.
+    if (n_it > 0) {
       constexpr uint32_t idesc_s = make_idesc(kFmt, 128, QT, false, false);
       constexpr uint32_t idesc_t = make_idesc(kFmt, 128, HD, false, true);
       const uint32_t aK = smem_u32(sK), aV = smem_u32(sV);
@@ -463,37 +479,57 @@ __global__ void __launch_bounds__(320, 1)
           umma_ts<kKind>(d, a_base + C::a_col(ks, HALF), mnmajor_desc<C::TF32>(b_tile, QT, ks, C::K_PER), idesc_t,
                          (acc || ks > 0) ? 1u : 0u);
       };
-      bool ok = mbar_wait(kv_full, 0, abort_flag, limit, 12) && mbar_wait(&q_full[0], 0, abort_flag, limit, 13);
+      bool ok = mbar_wait_warp(kv_full, 0, abort_flag, limit, 12) &&
+                mbar_wait_warp(&q_full[0], 0, abort_flag, limit, 13);
       if (ok) {
         tc_fence_after();
-        gemm_ss(tbase + C::KV_S, aK, smem_u32(sQ(0)));
-        umma_commit(s_full);
-        gemm_ss(tbase + C::KV_DP, aV, smem_u32(sdO(0)));
-        umma_commit(dp_full);
+        if (elect_one()) {
+          gemm_ss(tbase + C::KV_S, aK, smem_u32(sQ(0)));
+          umma_commit(s_full);
+          gemm_ss(tbase + C::kv_dp(0), aV, smem_u32(sdO(0)));
+          umma_commit(&dp_full[0]);
+        }
+        __syncwarp();
       }
+      // Double-buffered: S^T and dP^T of tile it+1 are queued before the
+      // dV/dK GEMMs of tile it, which wait for the compute warps.
       for (int it = 0; ok && it < n_it; ++it) {
         const int st = it % ST;
         const int st1 = (it + 1) % ST;
+        const int b = C::KV_DBL ? (it & 1) : 0;
         if (it + 1 < n_it) {
-          if (!(ok = mbar_wait(s_free, it & 1, abort_flag, limit, 14))) break;
-          if (!(ok = mbar_wait(&q_full[st1], ((it + 1) / ST) & 1, abort_flag, limit, 15))) break;
+          if (!(ok = mbar_wait_warp(s_free, it & 1, abort_flag, limit, 14))) break;
+          if (!(ok = mbar_wait_warp(&q_full[st1], ((it + 1) / ST) & 1, abort_flag, limit, 15))) break;
           tc_fence_after();
-          gemm_ss(tbase + C::KV_S, aK, smem_u32(sQ(st1)));
-          umma_commit(s_full);
+          if (elect_one()) {
+            gemm_ss(tbase + C::KV_S, aK, smem_u32(sQ(st1)));
+            umma_commit(s_full);
+            if constexpr (C::KV_DBL) {
+              gemm_ss(tbase + C::kv_dp(b ^ 1), aV, smem_u32(sdO(st1)));
+              umma_commit(&dp_full[b ^ 1]);
+            }
+          }
+          __syncwarp();
         }
-        if (!(ok = mbar_wait(p_full, it & 1, abort_flag, limit, 16))) break;
+        if (!(ok = mbar_wait_warp(&p_full[b], C::KV_DBL ? ((it >> 1) & 1) : (it & 1), abort_flag, limit, 16))) break;
         tc_fence_after();
-        gemm_ts(tbase + C::KV_DV, tbase + C::KV_P, smem_u32(sdOm(st)), it > 0);
-        gemm_ts(tbase + C::KV_DK, tbase + C::KV_DP, smem_u32(sQm(st)), it > 0);
-        umma_commit(&q_empty[st]);
-        if (it + 1 < n_it) {
-          gemm_ss(tbase + C::KV_DP, aV, smem_u32(sdO(st1)));
-          umma_commit(dp_full);
-        } else {
-          umma_commit(acc_full);
+        if (elect_one()) {
+          gemm_ts(tbase + C::KV_DV, tbase + C::kv_p(b), smem_u32(sdOm(st)), it > 0);
+          gemm_ts(tbase + C::KV_DK, tbase + C::kv_dp(b), smem_u32(sQm(st)), it > 0);
+          umma_commit(&q_empty[st]);
+          if (it + 1 < n_it) {
+            if constexpr (!C::KV_DBL) {
+              gemm_ss(tbase + C::kv_dp(0), aV, smem_u32(sdO(st1)));
+              umma_commit(&dp_full[0]);
+            }
+          } else {
+            umma_commit(acc_full);
+          }
         }
+        __syncwarp();
       }
-      umma_commit(done_bar);
+      if (elect_one()) umma_commit(done_bar);
+      __syncwarp();
       const uint64_t t0 = globaltimer_ns();
       while (!mbar_try_wait(done_bar, 0) && globaltimer_ns() - t0 < limit) {
       }
@@ -514,6 +550,8 @@ __global__ void __launch_bounds__(320, 1)
     const float* delta_bh = p.delta + (size_t)bh * p.Tq_pad;
     bool ok = true;
     for (int it = 0; it < n_it; ++it) {
+      const int b = C::KV_DBL ? (it & 1) : 0;
+      const uint32_t ph = C::KV_DBL ? ((it >> 1) & 1) : (it & 1);
       const int qtile0 = (qt_first + it) * QT;
       const int q0 = qtile0 + h * HALF;
       float L[HALF];
@@ -544,7 +582,7 @@ __global__ void __launch_bounds__(320, 1)
         for (int c = 0; c < HALF; ++c)
           if (c < cmin) s[c] = 0.f;
       }
-      if (!(ok = mbar_wait(dp_full, it & 1, abort_flag, limit, 18))) break;
+      if (!(ok = mbar_wait(&dp_full[b], ph, abort_flag, limit, 18))) break;
       tc_fence_after();
       // dS^T = P^T (dP^T - delta) * scale, 32 columns at a time, written in
       // place (tf32) or packed into the already-read front of the dP buffer.
@@ -553,7 +591,7 @@ __global__ void __launch_bounds__(320, 1)
         float dsv[32];
         {
           uint32_t regs[32];
-          tmem_ld32(tbase + lane_off + C::KV_DP + h * HALF + ch * 32, regs);
+          tmem_ld32(tbase + lane_off + C::kv_dp(b) + h * HALF + ch * 32, regs);
           tmem_wait_ld();
 #pragma unroll
           for (int c4 = 0; c4 < 8; ++c4) {
@@ -567,17 +605,14 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
         if constexpr (C::TF32)
-          tmem_store_operand<DT>(tbase + lane_off + C::KV_DP + h * HALF + ch * 32, dsv);
+          tmem_store_operand<DT>(tbase + lane_off + C::kv_dp(b) + h * HALF + ch * 32, dsv);
         else
-          tmem_store_operand<DT>(tbase + lane_off + C::KV_DP + h * HALF + ch * 16, dsv);
+          tmem_store_operand<DT>(tbase + lane_off + C::kv_dp(b) + h * HALF + ch * 16, dsv);
       }
-      if constexpr (C::TF32)
-        tmem_store_operand<DT>(tbase + lane_off + C::KV_P + h * HALF, s);
-      else
-        tmem_store_operand<DT>(tbase + lane_off + C::KV_DP + h * HALF + HALF / 2, s);
+      tmem_store_operand<DT>(tbase + lane_off + C::kv_p(b) + h * HALF, s);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[b]);
     }
     // ------------------------------ epilogue ------------------------------
     if (ok && n_it > 0) ok = mbar_wait(acc_full, 0, abort_flag, limit, 19);
@@ -641,9 +676,9 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* v_empty = v_full + ST;  // [ST]
   uint64_t* s_full = v_empty + ST;
   uint64_t* s_free = s_full + 1;
-  uint64_t* dp_full = s_free + 1;
-  uint64_t* ds_full = dp_full + 1;
-  uint64_t* acc_full = ds_full + 1;
+  uint64_t* dp_full = s_free + 1;  // [2] per dP buffer
+  uint64_t* ds_full = dp_full + 2;  // [2] per dP buffer
+  uint64_t* acc_full = ds_full + 2;
   uint64_t* done_bar = acc_full + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
@@ -675,8 +710,10 @@ __global__ void __launch_bounds__(320, 1)
     }
     mbar_init(s_full, 1);
     mbar_init(s_free, 256);
-    mbar_init(dp_full, 1);
-    mbar_init(ds_full, 256);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&dp_full[b], 1);
+      mbar_init(&ds_full[b], 256);
+    }
     mbar_init(acc_full, 1);
     mbar_init(done_bar, 1);
     *abort_flag = 0;
@@ -739,7 +776,8 @@ __global__ void __launch_bounds__(320, 1)
     }
     __syncwarp();
   } else if (warp == MMA_WARP) {
-    if (lane == 0 && n_kv > 0) {
+    // The whole warp runs this loop; one elected lane issues each MMA group.
+    if (n_kv > 0) {
       constexpr uint32_t idesc_s = make_idesc(kFmt, 128, KT, false, false);
       constexpr uint32_t idesc_t = make_idesc(kFmt, 128, HD, false, true);
       const uint32_t aQ = smem_u32(sQ), adO = smem_u32(sdO);
@@ -749,46 +787,76 @@ __global__ void __launch_bounds__(320, 1)
         for (int ks = 0; ks < C::KSTEP_S; ++ks)
           umma_ss<kKind>(d, kmajor_desc(a_tile, 128, ks), kmajor_desc(b_tile, KT, ks), idesc_s, ks > 0 ? 1u : 0u);
       };
-      bool ok = mbar_wait(q_full, 0, abort_flag, limit, 23) && mbar_wait(&k_full[0], 0, abort_flag, limit, 24) &&
-                mbar_wait(&v_full[0], 0, abort_flag, limit, 25);
+      bool ok = mbar_wait_warp(q_full, 0, abort_flag, limit, 23) &&
+                mbar_wait_warp(&k_full[0], 0, abort_flag, limit, 24) &&
+                mbar_wait_warp(&v_full[0], 0, abort_flag, limit, 25);
       if (ok) {
         tc_fence_after();
-        gemm_ss(tbase + C::Q_S, aQ, smem_u32(sK(0)));
-        umma_commit(s_full);
-        gemm_ss(tbase + C::Q_DP, adO, smem_u32(sV(0)));
-        umma_commit(dp_full);
-        umma_commit(&v_empty[0]);
+        if (elect_one()) {
+          gemm_ss(tbase + C::Q_S, aQ, smem_u32(sK(0)));
+          umma_commit(s_full);
+          gemm_ss(tbase + C::q_dp(0), adO, smem_u32(sV(0)));
+          umma_commit(&dp_full[0]);
+          umma_commit(&v_empty[0]);
+        }
+        __syncwarp();
       }
+      // Double-buffered: S and dP of key tile j+1 are queued before the dQ
+      // GEMM of tile j, which waits for the compute warps.
       for (int j = 0; ok && j < n_kv; ++j) {
         const int st = j % ST;
         const int st1 = (j + 1) % ST;
         const uint32_t ph1 = ((j + 1) / ST) & 1;
+        const int b = C::Q_DBL ? (j & 1) : 0;
         if (j + 1 < n_kv) {
-          if (!(ok = mbar_wait(s_free, j & 1, abort_flag, limit, 26))) break;
-          if (!(ok = mbar_wait(&k_full[st1], ph1, abort_flag, limit, 27))) break;
+          if (!(ok = mbar_wait_warp(s_free, j & 1, abort_flag, limit, 26))) break;
+          if (!(ok = mbar_wait_warp(&k_full[st1], ph1, abort_flag, limit, 27))) break;
           tc_fence_after();
-          gemm_ss(tbase + C::Q_S, aQ, smem_u32(sK(st1)));
-          umma_commit(s_full);
+          if (elect_one()) {
+            gemm_ss(tbase + C::Q_S, aQ, smem_u32(sK(st1)));
+            umma_commit(s_full);
+          }
+          __syncwarp();
+          if constexpr (C::Q_DBL) {
+            if (!(ok = mbar_wait_warp(&v_full[st1], ph1, abort_flag, limit, 29))) break;
+            tc_fence_after();
+            if (elect_one()) {
+              gemm_ss(tbase + C::q_dp(b ^ 1), adO, smem_u32(sV(st1)));
+              umma_commit(&dp_full[b ^ 1]);
+              umma_commit(&v_empty[st1]);
+            }
+            __syncwarp();
+          }
         }
-        if (!(ok = mbar_wait(ds_full, j & 1, abort_flag, limit, 28))) break;
+        if (!(ok = mbar_wait_warp(&ds_full[b], C::Q_DBL ? ((j >> 1) & 1) : (j & 1), abort_flag, limit, 28))) break;
         tc_fence_after();
-        const uint32_t bK = smem_u32(sKm(st));
+        if (elect_one()) {
+          const uint32_t bK = smem_u32(sKm(st));
 #pragma unroll
-        for (int ks = 0; ks < KT / C::K_PER; ++ks)
-          umma_ts<kKind>(tbase + C::Q_DQ, tbase + C::Q_DP + C::a_col(ks, HALF),
-                         mnmajor_desc<C::TF32>(bK, KT, ks, C::K_PER), idesc_t, (j > 0 || ks > 0) ? 1u : 0u);
-        umma_commit(&k_empty[st]);
+          for (int ks = 0; ks < KT / C::K_PER; ++ks)
+            umma_ts<kKind>(tbase + C::Q_DQ, tbase + C::q_dp(b) + C::a_col(ks, HALF),
+                           mnmajor_desc<C::TF32>(bK, KT, ks, C::K_PER), idesc_t, (j > 0 || ks > 0) ? 1u : 0u);
+          umma_commit(&k_empty[st]);
+        }
+        __syncwarp();
         if (j + 1 < n_kv) {
-          if (!(ok = mbar_wait(&v_full[st1], ph1, abort_flag, limit, 29))) break;
-          tc_fence_after();
-          gemm_ss(tbase + C::Q_DP, adO, smem_u32(sV(st1)));
-          umma_commit(dp_full);
-          umma_commit(&v_empty[st1]);
+          if constexpr (!C::Q_DBL) {
+            if (!(ok = mbar_wait_warp(&v_full[st1], ph1, abort_flag, limit, 29))) break;
+            tc_fence_after();
+            if (elect_one()) {
+              gemm_ss(tbase + C::q_dp(0), adO, smem_u32(sV(st1)));
+              umma_commit(&dp_full[0]);
+              umma_commit(&v_empty[st1]);
+            }
+            __syncwarp();
+          }
         } else {
-          umma_commit(acc_full);
+          if (elect_one()) umma_commit(acc_full);
+          __syncwarp();
         }
       }
-      umma_commit(done_bar);
+      if (elect_one()) umma_commit(done_bar);
+      __syncwarp();
       const uint64_t t0 = globaltimer_ns();
       while (!mbar_try_wait(done_bar, 0) && globaltimer_ns() - t0 < limit) {
       }
@@ -811,6 +879,8 @@ __global__ void __launch_bounds__(320, 1)
     if (!q_ok) vis = -1;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
+      const int b = C::Q_DBL ? (j & 1) : 0;
+      const uint32_t ph = C::Q_DBL ? ((j >> 1) & 1) : (j & 1);
       const int kc0 = j * KT + h * HALF;  // first key of this thread's half
       if (!(ok = mbar_wait(s_full, j & 1, abort_flag, limit, 30))) break;
       tc_fence_after();
@@ -826,16 +896,16 @@ __global__ void __launch_bounds__(320, 1)
         for (int c = 0; c < HALF; ++c)
           if (c > lim) s[c] = 0.f;
       }
-      if (!(ok = mbar_wait(dp_full, j & 1, abort_flag, limit, 31))) break;
+      if (!(ok = mbar_wait(&dp_full[b], ph, abort_flag, limit, 31))) break;
       tc_fence_after();
       float dsv[HALF];
-      tmem_load_row(tbase + lane_off + C::Q_DP + h * HALF, dsv);
+      tmem_load_row(tbase + lane_off + C::q_dp(b) + h * HALF, dsv);
 #pragma unroll
       for (int c = 0; c < HALF; ++c) dsv[c] = s[c] * (dsv[c] - dl) * scale;
-      tmem_store_operand<DT>(tbase + lane_off + C::Q_DP + h * HALF, dsv);
+      tmem_store_operand<DT>(tbase + lane_off + C::q_dp(b) + h * HALF, dsv);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(ds_full);
+      mbar_arrive(&ds_full[b]);
     }
     if (ok && n_kv > 0) ok = mbar_wait(acc_full, 0, abort_flag, limit, 32);
     if (ok) {

@@ -234,7 +234,8 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
     }
     __syncwarp();
   } else if (warp == MMA_WARP) {
-    if (lane == 0 && n_max > 0) {
+    // The whole warp runs this loop; one elected lane issues each MMA group.
+    if (n_max > 0) {
       constexpr uint32_t idesc_s = make_idesc(kFmt, 128, BN, false, false);
       constexpr uint32_t idesc_pv = make_idesc(kFmt, 128, HD, false, true);
       const uint32_t sQ_addr = smem_u32(sQ);
@@ -260,47 +261,60 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
         }
       };
 
-      bool ok = mbar_wait(q_full, 0, abort_flag, limit, 3);
-      if (ok) ok = mbar_wait(&k_full[0], 0, abort_flag, limit, 4);
+      bool ok = mbar_wait_warp(q_full, 0, abort_flag, limit, 3);
+      if (ok) ok = mbar_wait_warp(&k_full[0], 0, abort_flag, limit, 4);
       if (ok) {
         tc_fence_after();
+        if (elect_one()) {
 #pragma unroll
-        for (int k = 0; k < NQ; ++k) {
-          if (n_kv[k] > 0) {
-            issue_s(k, 0);
-            umma_commit(&s_full[k]);
+          for (int k = 0; k < NQ; ++k) {
+            if (n_kv[k] > 0) {
+              issue_s(k, 0);
+              umma_commit(&s_full[k]);
+            }
           }
+          umma_commit(&k_empty[0]);
         }
-        umma_commit(&k_empty[0]);
+        __syncwarp();
       }
       for (int j = 0; ok && j < n_max; ++j) {
         const int st = j % VST;
         const int st1 = (j + 1) % KST;
-        if (!(ok = mbar_wait(&v_full[st], (j / VST) & 1, abort_flag, limit, 5))) break;
+        if (!(ok = mbar_wait_warp(&v_full[st], (j / VST) & 1, abort_flag, limit, 5))) break;
         bool next_k = false;
 #pragma unroll
         for (int k = 0; k < NQ; ++k) {
           if (j >= n_kv[k]) continue;
-          if (!(ok = mbar_wait(&p_full[k], j & 1, abort_flag, limit, 6))) break;
+          if (!(ok = mbar_wait_warp(&p_full[k], j & 1, abort_flag, limit, 6))) break;
           tc_fence_after();
-          issue_pv(k, st, j > 0);
-          if (j == n_kv[k] - 1) umma_commit(&o_full[k]);
+          if (elect_one()) {
+            issue_pv(k, st, j > 0);
+            if (j == n_kv[k] - 1) umma_commit(&o_full[k]);
+          }
+          __syncwarp();
           if (j + 1 < n_kv[k]) {
             if (!next_k) {
-              if (!(ok = mbar_wait(&k_full[st1], ((j + 1) / KST) & 1, abort_flag, limit, 7))) break;
+              if (!(ok = mbar_wait_warp(&k_full[st1], ((j + 1) / KST) & 1, abort_flag, limit, 7))) break;
               tc_fence_after();
               next_k = true;
             }
-            issue_s(k, st1);
-            umma_commit(&s_full[k]);
+            if (elect_one()) {
+              issue_s(k, st1);
+              umma_commit(&s_full[k]);
+            }
+            __syncwarp();
           }
         }
-        umma_commit(&v_empty[st]);
-        if (next_k) umma_commit(&k_empty[st1]);
+        if (elect_one()) {
+          umma_commit(&v_empty[st]);
+          if (next_k) umma_commit(&k_empty[st1]);
+        }
+        __syncwarp();
       }
       // Wait (bounded, regardless of abort) for every MMA issued so far, so
       // that TMEM is idle before it is released.
-      umma_commit(done_bar);
+      if (elect_one()) umma_commit(done_bar);
+      __syncwarp();
       const uint64_t t0 = globaltimer_ns();
       while (!mbar_try_wait(done_bar, 0) && globaltimer_ns() - t0 < limit) {
       }

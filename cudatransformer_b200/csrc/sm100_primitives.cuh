@@ -104,6 +104,27 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// The same wait executed by every lane of a converged warp; the result is
+// warp-uniform (a failure on any lane fails all of them).
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                               uint64_t limit_ns, int site) {
+  const bool ok = mbar_wait(bar, parity, abort, limit_ns, site);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// True on exactly one lane of a converged warp (elect.sync).  tcgen05.mma is
+// issued by one thread; issuing it from a converged warp under this predicate
+// (instead of from a lone lane of a diverged warp) keeps the MMA stream fed
+// while the softmax / compute warps load the issue slots (measured: ~2.4x
+// more MMA issue throughput under full ALU load on the other warps).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // ---------------------------------------------------------------------------
 // TMA (no multicast anywhere in this project: every CTA fetches its own tiles)
 // ---------------------------------------------------------------------------
