@@ -178,25 +178,35 @@ struct BwdConfig {
   // dK/dV kernel: 128 stationary keys (MMA M); streamed query tiles of KV_QT rows.
   static constexpr int KV_KEYS = 128;
   static constexpr int KV_QT = TF32 ? 64 : 128;
-  // dQ kernel: 128 stationary queries; streamed key tiles of Q_KT rows.
+  // dQ kernel: 128 stationary queries; streamed key tiles of Q_KT rows (128:
+  // N=128 MMAs run at ~1.7x the per-MAC rate of N=64 ones, and the per-tile
+  // barrier / TMEM round trips are amortised over twice the keys).
   static constexpr int Q_ROWS = 128;
-  static constexpr int Q_KT = TF32 ? 64 : 128;
+  static constexpr int Q_KT = (TF32 && HD > 64) ? 64 : 128;
   // tf32 operands read both K-major and MN-major get a second copy in the
   // 32-byte-granule swizzle; 16-bit operands serve both from one buffer.
   static constexpr int BIG_TILE = 128 * ROW_BYTES;
   static constexpr int KV_QTILE = KV_QT * ROW_BYTES;
   static constexpr int Q_KTILE = Q_KT * ROW_BYTES;
   static constexpr int KV_STAGE_BYTES = (TF32 ? 4 : 2) * KV_QTILE;  // Q, dO (+ MN copies)
-  static constexpr int Q_STAGE_BYTES = (TF32 ? 3 : 2) * Q_KTILE;    // K, V (+ K MN copy)
+  static constexpr int Q_KSTAGE_BYTES = (TF32 ? 2 : 1) * Q_KTILE;   // K (+ K MN copy)
+  static constexpr int Q_VSTAGE_BYTES = Q_KTILE;                    // V
   static constexpr int BUDGET = 216 * 1024;
   static constexpr int KV_ST = (BUDGET - 2 * BIG_TILE) / KV_STAGE_BYTES > 3 ? 3 : (BUDGET - 2 * BIG_TILE) / KV_STAGE_BYTES;
-  static constexpr int Q_ST = (BUDGET - 2 * BIG_TILE) / Q_STAGE_BYTES > 3 ? 3 : (BUDGET - 2 * BIG_TILE) / Q_STAGE_BYTES;
+  // dQ kernel rings: K (+ its MN copy) and V separately.  tf32 at 128-key
+  // tiles: two K stages (the next S needs K(j+1) while dQ(j) still reads
+  // Km(j)) and one V stage (V(j+1) loads while dQ(j) runs, before dP(j+1)).
+  static constexpr int Q_BUDGET = 226 * 1024;
+  static constexpr int Q_PAIR = (Q_BUDGET - 2 * BIG_TILE) / (Q_KSTAGE_BYTES + Q_VSTAGE_BYTES);
+  static constexpr int Q_KST = TF32 ? 2 : (Q_PAIR > 3 ? 3 : Q_PAIR);
+  static constexpr int Q_VST = TF32 ? 1 : Q_KST;
   // dK/dV kernel TMEM map (columns, lanes = keys).  One buffer holds dP^T,
   // then dS^T (tf32: in place, P^T in the next KV_QT columns; 16-bit: dS^T|P^T
   // packed per half).  With KV_DBL the buffer is doubled so that the next dP^T
-  // GEMM is queued before the compute warps release the current one.  Off:
-  // measured 4-5% slower on B200 at both tf32 D=64 and bf16 shapes (the early
-  // dP^T delays the dV/dK GEMMs the compute warps are waiting behind).
+  // GEMM is queued before the compute warps release the current one, and the
+  // compute warps read S^T and dP^T with one TMEM round trip (tf32 only).  Off:
+  // measured 4-8% slower.  Thread-side TMEM loads/stores take ~4x longer while
+  // the tensor pipe is busy, and the early dP^T puts them under a running MMA.
   static constexpr int KV_HALF = KV_QT / 2;  // score columns per compute warpgroup
   static constexpr int KV_S = 0;
   static constexpr int KV_BUF = TF32 ? 2 * KV_QT : KV_QT;
@@ -209,7 +219,8 @@ struct BwdConfig {
   __host__ __device__ static constexpr int kv_p(int b) { return TF32 ? kv_dp(b) + KV_QT : kv_dp(b) + KV_HALF / 2; }
   // dQ kernel TMEM map (lanes = queries): S, then a dP buffer (dS after the
   // compute pass: tf32 in place, 16-bit packed per half), doubled with Q_DBL
-  // (off, for the same measured reason as KV_DBL), then the dQ accumulator.
+  // (off, measured slower for the reason given at KV_DBL), then the dQ
+  // accumulator.
   static constexpr int Q_HALF = Q_KT / 2;
   static constexpr int Q_S = 0;
   static constexpr bool Q_DBL = false;
@@ -219,9 +230,10 @@ struct BwdConfig {
   __host__ __device__ static constexpr int q_dp(int b) { return Q_KT + b * Q_KT; }
   static constexpr int NUM_BARS = 32;
   static constexpr int KV_SMEM = 1024 + 2 * BIG_TILE + KV_ST * KV_STAGE_BYTES + NUM_BARS * 8 + 16;
-  static constexpr int Q_SMEM = 1024 + 2 * BIG_TILE + Q_ST * Q_STAGE_BYTES + NUM_BARS * 8 + 16;
+  static constexpr int Q_SMEM = 1024 + 2 * BIG_TILE + Q_KST * Q_KSTAGE_BYTES + Q_VST * Q_VSTAGE_BYTES + NUM_BARS * 8 + 16;
   static constexpr int THREADS = 320;
-  static_assert(KV_ST >= 1 && Q_ST >= 1, "shared memory budget");
+  static_assert(KV_ST >= 1 && Q_KST >= 1 && Q_VST >= 1, "shared memory budget");
+  static_assert(Q_SMEM <= 232448, "dQ kernel shared memory");
   static_assert(KV_DV + HD <= 512 && Q_DQ + HD <= 512, "TMEM budget");
   static_assert(!KV_DBL || KV_QT + 2 * KV_BUF + 2 * HD <= 512, "TMEM budget (double-buffered dP^T)");
   static_assert(HD * EB % 128 == 0, "head dim must fill whole 128-byte rows");
@@ -243,6 +255,16 @@ __device__ __forceinline__ void tmem_load_row(uint32_t taddr, float (&v)[N]) {
 #pragma unroll
   for (int c = 0; c < N / 32; ++c) tmem_ld32f(taddr + c * 32, v + c * 32);
   tmem_wait_ld();
+}
+
+// Issue the loads of `N` fp32 TMEM columns into v[] without waiting for them
+// (tcgen05.wait::ld before use).  Thread-side TMEM accesses are slow while the
+// tensor pipe is busy (measured ~4x the idle latency), so loads that are ready
+// together are issued together and waited for once.
+template <int N>
+__device__ __forceinline__ void tmem_load_row_async(uint32_t taddr, float (&v)[N]) {
+#pragma unroll
+  for (int c = 0; c < N / 32; ++c) tmem_ld32f(taddr + c * 32, v + c * 32);
 }
 
 // Store v[] as an MMA A operand: tf32 (one column per value, rounded to
@@ -564,9 +586,21 @@ __global__ void __launch_bounds__(320, 1)
         L[4 * c + 3] = v4.w;
       }
       if (!(ok = mbar_wait(s_full, it & 1, abort_flag, limit, 17))) break;
-      tc_fence_after();
       float s[HALF];
-      tmem_load_row(tbase + lane_off + C::KV_S + h * HALF, s);
+      // kBatch: S^T and dP^T were queued together (double-buffered dP^T) and
+      // fit the registers: read both with one TMEM round trip.
+      constexpr bool kBatch = C::KV_DBL && HALF == 32;
+      uint32_t dpre[32];
+      if constexpr (kBatch) {
+        if (!(ok = mbar_wait(&dp_full[b], ph, abort_flag, limit, 18))) break;
+        tc_fence_after();
+        tmem_load_row_async(tbase + lane_off + C::KV_S + h * HALF, s);
+        tmem_ld32(tbase + lane_off + C::kv_dp(b) + h * HALF, dpre);
+        tmem_wait_ld();
+      } else {
+        tc_fence_after();
+        tmem_load_row(tbase + lane_off + C::KV_S + h * HALF, s);
+      }
       tc_fence_before();
       mbar_arrive(s_free);
       // P^T = exp2(S^T * scale*log2e - lse*log2e); padding queries have lse = +inf
@@ -582,8 +616,10 @@ __global__ void __launch_bounds__(320, 1)
         for (int c = 0; c < HALF; ++c)
           if (c < cmin) s[c] = 0.f;
       }
-      if (!(ok = mbar_wait(&dp_full[b], ph, abort_flag, limit, 18))) break;
-      tc_fence_after();
+      if constexpr (!kBatch) {
+        if (!(ok = mbar_wait(&dp_full[b], ph, abort_flag, limit, 18))) break;
+        tc_fence_after();
+      }
       // dS^T = P^T (dP^T - delta) * scale, 32 columns at a time, written in
       // place (tf32) or packed into the already-read front of the dP buffer.
 #pragma unroll
@@ -591,8 +627,13 @@ __global__ void __launch_bounds__(320, 1)
         float dsv[32];
         {
           uint32_t regs[32];
-          tmem_ld32(tbase + lane_off + C::kv_dp(b) + h * HALF + ch * 32, regs);
-          tmem_wait_ld();
+          if constexpr (kBatch) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) regs[i] = dpre[i];
+          } else {
+            tmem_ld32(tbase + lane_off + C::kv_dp(b) + h * HALF + ch * 32, regs);
+            tmem_wait_ld();
+          }
 #pragma unroll
           for (int c4 = 0; c4 < 8; ++c4) {
             const float4 d4 = __ldg(reinterpret_cast<const float4*>(delta_bh + q0 + ch * 32) + c4);
@@ -653,7 +694,8 @@ __global__ void __launch_bounds__(320, 1)
                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                       const __grid_constant__ CUtensorMap tm_km, const BwdParams p, int n_qtiles) {
   using C = BwdConfig<DT, HD>;
-  constexpr int ST = C::Q_ST;
+  constexpr int KST = C::Q_KST;
+  constexpr int VST = C::Q_VST;
   constexpr int KT = C::Q_KT;
   constexpr int HALF = C::Q_HALF;
   constexpr int kKind = DTypeTraits<DT>::kKind;
@@ -664,17 +706,18 @@ __global__ void __launch_bounds__(320, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
   uint8_t* sdO = sQ + C::BIG_TILE;
-  uint8_t* sStage = sdO + C::BIG_TILE;  // per stage: K, V [, K MN copy]
-  auto sK = [&](int st) { return sStage + st * C::Q_STAGE_BYTES; };
-  auto sV = [&](int st) { return sStage + st * C::Q_STAGE_BYTES + C::Q_KTILE; };
-  auto sKm = [&](int st) { return C::TF32 ? sStage + st * C::Q_STAGE_BYTES + 2 * C::Q_KTILE : sK(st); };
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + ST * C::Q_STAGE_BYTES);
+  uint8_t* sKring = sdO + C::BIG_TILE;  // per stage: K [, K MN copy]
+  uint8_t* sVring = sKring + KST * C::Q_KSTAGE_BYTES;
+  auto sK = [&](int st) { return sKring + st * C::Q_KSTAGE_BYTES; };
+  auto sKm = [&](int st) { return C::TF32 ? sKring + st * C::Q_KSTAGE_BYTES + C::Q_KTILE : sK(st); };
+  auto sV = [&](int st) { return sVring + st * C::Q_VSTAGE_BYTES; };
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sVring + VST * C::Q_VSTAGE_BYTES);
   uint64_t* q_full = bars;
-  uint64_t* k_full = q_full + 1;    // [ST]
-  uint64_t* k_empty = k_full + ST;  // [ST]
-  uint64_t* v_full = k_empty + ST;  // [ST]
-  uint64_t* v_empty = v_full + ST;  // [ST]
-  uint64_t* s_full = v_empty + ST;
+  uint64_t* k_full = q_full + 1;     // [KST]
+  uint64_t* k_empty = k_full + KST;  // [KST]
+  uint64_t* v_full = k_empty + KST;  // [VST]
+  uint64_t* v_empty = v_full + VST;  // [VST]
+  uint64_t* s_full = v_empty + VST;
   uint64_t* s_free = s_full + 1;
   uint64_t* dp_full = s_free + 1;  // [2] per dP buffer
   uint64_t* ds_full = dp_full + 2;  // [2] per dP buffer
@@ -702,9 +745,11 @@ __global__ void __launch_bounds__(320, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < ST; ++s) {
+    for (int s = 0; s < KST; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < VST; ++s) {
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
@@ -744,33 +789,32 @@ __global__ void __launch_bounds__(320, 1)
       }
       int issued_k = 0, issued_v = 0;
       for (int j = 0; j < n_kv; ++j) {
-        const int st = j % ST;
-        const uint32_t ph = (j / ST) & 1;
+        const int kst = j % KST, vst = j % VST;
         const int row = p.k_row0 + j * KT;
-        if (!mbar_wait(&k_empty[st], ph ^ 1, abort_flag, limit, 21)) break;
-        mbar_arrive_expect_tx(&k_full[st], (C::TF32 ? 2 : 1) * C::Q_KTILE);
+        if (!mbar_wait(&k_empty[kst], ((j / KST) & 1) ^ 1, abort_flag, limit, 21)) break;
+        mbar_arrive_expect_tx(&k_full[kst], C::Q_KSTAGE_BYTES);
 #pragma unroll
         for (int b = 0; b < C::KBLK; ++b) {
-          tma_load_3d(sK(st) + b * KT * 128, &tm_k, &k_full[st], b * C::E128, row, bh);
-          if constexpr (C::TF32) tma_load_3d(sKm(st) + b * KT * 128, &tm_km, &k_full[st], b * C::E128, row, bh);
+          tma_load_3d(sK(kst) + b * KT * 128, &tm_k, &k_full[kst], b * C::E128, row, bh);
+          if constexpr (C::TF32) tma_load_3d(sKm(kst) + b * KT * 128, &tm_km, &k_full[kst], b * C::E128, row, bh);
         }
         issued_k = j + 1;
-        if (!mbar_wait(&v_empty[st], ph ^ 1, abort_flag, limit, 22)) break;
-        mbar_arrive_expect_tx(&v_full[st], C::Q_KTILE);
+        if (!mbar_wait(&v_empty[vst], ((j / VST) & 1) ^ 1, abort_flag, limit, 22)) break;
+        mbar_arrive_expect_tx(&v_full[vst], C::Q_VSTAGE_BYTES);
 #pragma unroll
         for (int b = 0; b < C::KBLK; ++b)
-          tma_load_3d(sV(st) + b * KT * 128, &tm_v, &v_full[st], b * C::E128, row, bh);
+          tma_load_3d(sV(vst) + b * KT * 128, &tm_v, &v_full[vst], b * C::E128, row, bh);
         issued_v = j + 1;
       }
       if (*abort_flag) {
         const uint64_t t0 = globaltimer_ns();
         while (!mbar_try_wait(q_full, 0) && globaltimer_ns() - t0 < limit) {
         }
-        for (int j = max(0, issued_k - ST); j < issued_k; ++j)
-          while (!mbar_try_wait(&k_full[j % ST], (j / ST) & 1) && globaltimer_ns() - t0 < limit) {
+        for (int j = max(0, issued_k - KST); j < issued_k; ++j)
+          while (!mbar_try_wait(&k_full[j % KST], (j / KST) & 1) && globaltimer_ns() - t0 < limit) {
           }
-        for (int j = max(0, issued_v - ST); j < issued_v; ++j)
-          while (!mbar_try_wait(&v_full[j % ST], (j / ST) & 1) && globaltimer_ns() - t0 < limit) {
+        for (int j = max(0, issued_v - VST); j < issued_v; ++j)
+          while (!mbar_try_wait(&v_full[j % VST], (j / VST) & 1) && globaltimer_ns() - t0 < limit) {
           }
       }
     }
@@ -804,9 +848,11 @@ __global__ void __launch_bounds__(320, 1)
       // Double-buffered: S and dP of key tile j+1 are queued before the dQ
       // GEMM of tile j, which waits for the compute warps.
       for (int j = 0; ok && j < n_kv; ++j) {
-        const int st = j % ST;
-        const int st1 = (j + 1) % ST;
-        const uint32_t ph1 = ((j + 1) / ST) & 1;
+        const int st = j % KST;
+        const int st1 = (j + 1) % KST;
+        const uint32_t ph1 = ((j + 1) / KST) & 1;
+        const int vst1 = (j + 1) % VST;
+        const uint32_t vph1 = ((j + 1) / VST) & 1;
         const int b = C::Q_DBL ? (j & 1) : 0;
         if (j + 1 < n_kv) {
           if (!(ok = mbar_wait_warp(s_free, j & 1, abort_flag, limit, 26))) break;
@@ -818,12 +864,12 @@ __global__ void __launch_bounds__(320, 1)
           }
           __syncwarp();
           if constexpr (C::Q_DBL) {
-            if (!(ok = mbar_wait_warp(&v_full[st1], ph1, abort_flag, limit, 29))) break;
+            if (!(ok = mbar_wait_warp(&v_full[vst1], vph1, abort_flag, limit, 29))) break;
             tc_fence_after();
             if (elect_one()) {
-              gemm_ss(tbase + C::q_dp(b ^ 1), adO, smem_u32(sV(st1)));
+              gemm_ss(tbase + C::q_dp(b ^ 1), adO, smem_u32(sV(vst1)));
               umma_commit(&dp_full[b ^ 1]);
-              umma_commit(&v_empty[st1]);
+              umma_commit(&v_empty[vst1]);
             }
             __syncwarp();
           }
@@ -841,12 +887,12 @@ __global__ void __launch_bounds__(320, 1)
         __syncwarp();
         if (j + 1 < n_kv) {
           if constexpr (!C::Q_DBL) {
-            if (!(ok = mbar_wait_warp(&v_full[st1], ph1, abort_flag, limit, 29))) break;
+            if (!(ok = mbar_wait_warp(&v_full[vst1], vph1, abort_flag, limit, 29))) break;
             tc_fence_after();
             if (elect_one()) {
-              gemm_ss(tbase + C::q_dp(0), adO, smem_u32(sV(st1)));
+              gemm_ss(tbase + C::q_dp(0), adO, smem_u32(sV(vst1)));
               umma_commit(&dp_full[0]);
-              umma_commit(&v_empty[st1]);
+              umma_commit(&v_empty[vst1]);
             }
             __syncwarp();
           }
@@ -883,9 +929,19 @@ __global__ void __launch_bounds__(320, 1)
       const uint32_t ph = C::Q_DBL ? ((j >> 1) & 1) : (j & 1);
       const int kc0 = j * KT + h * HALF;  // first key of this thread's half
       if (!(ok = mbar_wait(s_full, j & 1, abort_flag, limit, 30))) break;
-      tc_fence_after();
       float s[HALF];
-      tmem_load_row(tbase + lane_off + C::Q_S + h * HALF, s);
+      float dsv[HALF];
+      if constexpr (C::Q_DBL) {
+        // S and dP of this tile were queued together: one TMEM round trip
+        if (!(ok = mbar_wait(&dp_full[b], ph, abort_flag, limit, 31))) break;
+        tc_fence_after();
+        tmem_load_row_async(tbase + lane_off + C::Q_S + h * HALF, s);
+        tmem_load_row_async(tbase + lane_off + C::q_dp(b) + h * HALF, dsv);
+        tmem_wait_ld();
+      } else {
+        tc_fence_after();
+        tmem_load_row(tbase + lane_off + C::Q_S + h * HALF, s);
+      }
       tc_fence_before();
       mbar_arrive(s_free);
       const int lim = vis - kc0;  // columns > lim are masked (diagonal / tail tiles only)
@@ -896,10 +952,11 @@ __global__ void __launch_bounds__(320, 1)
         for (int c = 0; c < HALF; ++c)
           if (c > lim) s[c] = 0.f;
       }
-      if (!(ok = mbar_wait(&dp_full[b], ph, abort_flag, limit, 31))) break;
-      tc_fence_after();
-      float dsv[HALF];
-      tmem_load_row(tbase + lane_off + C::q_dp(b) + h * HALF, dsv);
+      if constexpr (!C::Q_DBL) {
+        if (!(ok = mbar_wait(&dp_full[b], ph, abort_flag, limit, 31))) break;
+        tc_fence_after();
+        tmem_load_row(tbase + lane_off + C::q_dp(b) + h * HALF, dsv);
+      }
 #pragma unroll
       for (int c = 0; c < HALF; ++c) dsv[c] = s[c] * (dsv[c] - dl) * scale;
       tmem_store_operand<DT>(tbase + lane_off + C::q_dp(b) + h * HALF, dsv);
