@@ -218,14 +218,11 @@ struct BwdConfig {
   __host__ __device__ static constexpr int kv_dp(int b) { return KV_QT + b * KV_BUF; }
   __host__ __device__ static constexpr int kv_p(int b) { return TF32 ? kv_dp(b) + KV_QT : kv_dp(b) + KV_HALF / 2; }
   // dQ kernel TMEM map (lanes = queries): S, then a dP buffer (dS after the
-  // compute pass: tf32 in place, 16-bit packed per half), doubled with Q_DBL
-  // (off, measured slower for the reason given at KV_DBL), then the dQ
+  // compute pass: tf32 in place, 16-bit packed per half), then the dQ
   // accumulator.
   static constexpr int Q_HALF = Q_KT / 2;
   static constexpr int Q_S = 0;
-  static constexpr bool Q_DBL = false;
-  static constexpr int Q_NBUF = Q_DBL ? 2 : 1;
-  static constexpr int Q_DQ = Q_KT + Q_NBUF * Q_KT;
+  static constexpr int Q_DQ = 2 * Q_KT;
   static constexpr uint32_t Q_TMEM = tmem_cols_for(Q_DQ + HD);
   __host__ __device__ static constexpr int q_dp(int b) { return Q_KT + b * Q_KT; }
   static constexpr int NUM_BARS = 32;
@@ -685,14 +682,69 @@ __global__ void __launch_bounds__(320, 1)
   }
 }
 
+// Load `COLS` fp32 TMEM columns of this thread's lane into registers (one
+// wait for all of them).
+template <int COLS>
+__device__ __forceinline__ void tmem_row_load(uint32_t taddr, uint32_t (&r)[COLS]) {
+#pragma unroll
+  for (int c = 0; c < COLS / 32; ++c) tmem_ld32(taddr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(r + c * 32));
+  tmem_wait_ld();
+}
+
+// Write a row of COLS fp32 values (register bits) to global memory: as DT, or
+// added into an fp32 row (`accumulate`, block entry points).
+template <typename DT, int COLS>
+__device__ __forceinline__ void row_store(const uint32_t (&r)[COLS], void* dst, bool accumulate) {
+  if (accumulate) {
+    float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+    for (int i = 0; i < COLS / 4; ++i) {
+      float4 a = d4[i];
+      a.x += __uint_as_float(r[4 * i]);
+      a.y += __uint_as_float(r[4 * i + 1]);
+      a.z += __uint_as_float(r[4 * i + 2]);
+      a.w += __uint_as_float(r[4 * i + 3]);
+      d4[i] = a;
+    }
+  } else if constexpr (sizeof(DT) == 4) {
+    float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+    for (int i = 0; i < COLS / 4; ++i)
+      d4[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]), __uint_as_float(r[4 * i + 2]),
+                          __uint_as_float(r[4 * i + 3]));
+  } else {
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int i = 0; i < COLS / 8; ++i) {
+      uint32_t w[4];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float a = __uint_as_float(r[8 * i + 2 * h]);
+        const float b = __uint_as_float(r[8 * i + 2 * h + 1]);
+        w[h] = std::is_same<DT, __nv_bfloat16>::value ? pack_bf16x2(a, b) : pack_f16x2(a, b);
+      }
+      d4[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
+// Work item `w` (round-major over a heavy-first order) handled by CTA `c` in
+// round `r` of a boustrophedon assignment: even rounds left to right, odd
+// rounds right to left.  With items sorted by decreasing cost this balances
+// persistent CTAs as well as dynamic scheduling does for these grids.
+__device__ __forceinline__ int snake_item(int r, int c, int G) { return r * G + ((r & 1) ? (G - 1 - c) : c); }
+
 // ---------------------------------------------------------------------------
-// dQ: one CTA per (128-query tile, batch*head)
+// dQ: persistent CTAs; each walks (128-query tile, batch*head) items, heavy
+// first.  Q/dO of the next item load while the current item's last tiles run;
+// the dQ accumulator is read into registers and released before it is written
+// out, so the next item's GEMMs start under the current item's epilogue.
 // ---------------------------------------------------------------------------
 template <typename DT, int HD>
 __global__ void __launch_bounds__(320, 1)
     attn_bwd_dq_sm100(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                      const __grid_constant__ CUtensorMap tm_km, const BwdParams p, int n_qtiles) {
+                      const __grid_constant__ CUtensorMap tm_km, const BwdParams p, int n_qtiles, int n_items) {
   using C = BwdConfig<DT, HD>;
   constexpr int KST = C::Q_KST;
   constexpr int VST = C::Q_VST;
@@ -713,38 +765,41 @@ __global__ void __launch_bounds__(320, 1)
   auto sV = [&](int st) { return sVring + st * C::Q_VSTAGE_BYTES; };
   uint64_t* bars = reinterpret_cast<uint64_t*>(sVring + VST * C::Q_VSTAGE_BYTES);
   uint64_t* q_full = bars;
-  uint64_t* k_full = q_full + 1;     // [KST]
+  uint64_t* q_empty = q_full + 1;
+  uint64_t* k_full = q_empty + 1;    // [KST]
   uint64_t* k_empty = k_full + KST;  // [KST]
   uint64_t* v_full = k_empty + KST;  // [VST]
   uint64_t* v_empty = v_full + VST;  // [VST]
   uint64_t* s_full = v_empty + VST;
   uint64_t* s_free = s_full + 1;
-  uint64_t* dp_full = s_free + 1;  // [2] per dP buffer
-  uint64_t* ds_full = dp_full + 2;  // [2] per dP buffer
-  uint64_t* acc_full = ds_full + 2;
-  uint64_t* done_bar = acc_full + 1;
+  uint64_t* dp_full = s_free + 1;
+  uint64_t* ds_full = dp_full + 1;
+  uint64_t* acc_full = ds_full + 1;
+  uint64_t* acc_free = acc_full + 1;
+  uint64_t* done_bar = acc_free + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  int qt, bh;
-  if (p.causal) {  // heavy query tiles first
-    qt = n_qtiles - 1 - (int)(blockIdx.x / p.BH);
-    bh = (int)(blockIdx.x % p.BH);
-  } else {
-    qt = (int)(blockIdx.x % n_qtiles);
-    bh = (int)(blockIdx.x / n_qtiles);
-  }
+  const int G = (int)gridDim.x, cta = (int)blockIdx.x;
   const int n_kv_all = (p.Tk + KT - 1) / KT;
-  int n_kv = n_kv_all;
-  if (p.causal) {
-    const int last_row = min(qt * C::Q_ROWS + C::Q_ROWS - 1, p.Tq - 1) + p.causal_offset;
-    n_kv = last_row < 0 ? 0 : min(n_kv_all, last_row / KT + 1);
-  }
+  // item -> query tile, batch*head, number of key tiles it sees
+  auto item = [&](int w, int& qt, int& bh) -> int {
+    if (p.causal) {  // heavy query tiles first
+      qt = n_qtiles - 1 - w / p.BH;
+      bh = w % p.BH;
+      const int last_row = min(qt * C::Q_ROWS + C::Q_ROWS - 1, p.Tq - 1) + p.causal_offset;
+      return last_row < 0 ? 0 : min(n_kv_all, last_row / KT + 1);
+    }
+    qt = w % n_qtiles;
+    bh = w / n_qtiles;
+    return n_kv_all;
+  };
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int s = 0; s < KST; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
@@ -755,11 +810,10 @@ __global__ void __launch_bounds__(320, 1)
     }
     mbar_init(s_full, 1);
     mbar_init(s_free, 256);
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&dp_full[b], 1);
-      mbar_init(&ds_full[b], 256);
-    }
+    mbar_init(dp_full, 1);
+    mbar_init(ds_full, 256);
     mbar_init(acc_full, 1);
+    mbar_init(acc_free, 256);
     mbar_init(done_bar, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -775,41 +829,58 @@ __global__ void __launch_bounds__(320, 1)
   const uint64_t limit = p.wait_limit_ns;
 
   if (warp == TMA_WARP) {
-    if (lane == 0 && n_kv > 0) {
+    if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
       tma_prefetch_desc(&tm_do);
-      const int qrow = p.q_row0 + qt * C::Q_ROWS;
-      mbar_arrive_expect_tx(q_full, 2 * C::BIG_TILE);
-#pragma unroll
-      for (int b = 0; b < C::KBLK; ++b) {
-        tma_load_3d(sQ + b * 128 * 128, &tm_q, q_full, b * C::E128, qrow, bh);
-        tma_load_3d(sdO + b * 128 * 128, &tm_do, q_full, b * C::E128, qrow, bh);
-      }
-      int issued_k = 0, issued_v = 0;
-      for (int j = 0; j < n_kv; ++j) {
-        const int kst = j % KST, vst = j % VST;
-        const int row = p.k_row0 + j * KT;
-        if (!mbar_wait(&k_empty[kst], ((j / KST) & 1) ^ 1, abort_flag, limit, 21)) break;
-        mbar_arrive_expect_tx(&k_full[kst], C::Q_KSTAGE_BYTES);
+      int g = 0, ni = 0;  // key tiles and non-empty items issued so far
+      int issued_q = 0, issued_k = 0, issued_v = 0;
+      bool ok = true;
+      for (int r = 0; ok; ++r) {
+        const int w = snake_item(r, cta, G);
+        if (r * G >= n_items) break;
+        if (w >= n_items) continue;
+        int qt, bh;
+        const int n_kv = item(w, qt, bh);
+        if (n_kv == 0) continue;
+        // Q/dO buffers are free once the previous item's last S/dP GEMMs ran
+        if (!(ok = mbar_wait(q_empty, (ni & 1) ^ 1, abort_flag, limit, 20))) break;
+        const int qrow = p.q_row0 + qt * C::Q_ROWS;
+        mbar_arrive_expect_tx(q_full, 2 * C::BIG_TILE);
 #pragma unroll
         for (int b = 0; b < C::KBLK; ++b) {
-          tma_load_3d(sK(kst) + b * KT * 128, &tm_k, &k_full[kst], b * C::E128, row, bh);
-          if constexpr (C::TF32) tma_load_3d(sKm(kst) + b * KT * 128, &tm_km, &k_full[kst], b * C::E128, row, bh);
+          tma_load_3d(sQ + b * 128 * 128, &tm_q, q_full, b * C::E128, qrow, bh);
+          tma_load_3d(sdO + b * 128 * 128, &tm_do, q_full, b * C::E128, qrow, bh);
         }
-        issued_k = j + 1;
-        if (!mbar_wait(&v_empty[vst], ((j / VST) & 1) ^ 1, abort_flag, limit, 22)) break;
-        mbar_arrive_expect_tx(&v_full[vst], C::Q_VSTAGE_BYTES);
+        issued_q = ni + 1;
+        for (int j = 0; j < n_kv; ++j, ++g) {
+          const int kst = g % KST, vst = g % VST;
+          const int row = p.k_row0 + j * KT;
+          if (!(ok = mbar_wait(&k_empty[kst], ((g / KST) & 1) ^ 1, abort_flag, limit, 21))) break;
+          mbar_arrive_expect_tx(&k_full[kst], C::Q_KSTAGE_BYTES);
 #pragma unroll
-        for (int b = 0; b < C::KBLK; ++b)
-          tma_load_3d(sV(vst) + b * KT * 128, &tm_v, &v_full[vst], b * C::E128, row, bh);
-        issued_v = j + 1;
+          for (int b = 0; b < C::KBLK; ++b) {
+            tma_load_3d(sK(kst) + b * KT * 128, &tm_k, &k_full[kst], b * C::E128, row, bh);
+            if constexpr (C::TF32) tma_load_3d(sKm(kst) + b * KT * 128, &tm_km, &k_full[kst], b * C::E128, row, bh);
+          }
+          issued_k = g + 1;
+          if (!(ok = mbar_wait(&v_empty[vst], ((g / VST) & 1) ^ 1, abort_flag, limit, 22))) break;
+          mbar_arrive_expect_tx(&v_full[vst], C::Q_VSTAGE_BYTES);
+#pragma unroll
+          for (int b = 0; b < C::KBLK; ++b)
+            tma_load_3d(sV(vst) + b * KT * 128, &tm_v, &v_full[vst], b * C::E128, row, bh);
+          issued_v = g + 1;
+        }
+        ++ni;
       }
+      // On an aborted run some loads may still be landing: wait (bounded,
+      // ignoring the abort flag) for the last load issued into each buffer.
       if (*abort_flag) {
         const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(q_full, 0) && globaltimer_ns() - t0 < limit) {
-        }
+        if (issued_q > 0)
+          while (!mbar_try_wait(q_full, (issued_q - 1) & 1) && globaltimer_ns() - t0 < limit) {
+          }
         for (int j = max(0, issued_k - KST); j < issued_k; ++j)
           while (!mbar_try_wait(&k_full[j % KST], (j / KST) & 1) && globaltimer_ns() - t0 < limit) {
           }
@@ -821,161 +892,174 @@ __global__ void __launch_bounds__(320, 1)
     __syncwarp();
   } else if (warp == MMA_WARP) {
     // The whole warp runs this loop; one elected lane issues each MMA group.
-    if (n_kv > 0) {
-      constexpr uint32_t idesc_s = make_idesc(kFmt, 128, KT, false, false);
-      constexpr uint32_t idesc_t = make_idesc(kFmt, 128, HD, false, true);
-      const uint32_t aQ = smem_u32(sQ), adO = smem_u32(sdO);
-      // S = Q K^T, dP = dO V^T: A is the 128-query tile, B the streamed key tile.
-      auto gemm_ss = [&](uint32_t d, uint32_t a_tile, uint32_t b_tile) {
+    constexpr uint32_t idesc_s = make_idesc(kFmt, 128, KT, false, false);
+    constexpr uint32_t idesc_t = make_idesc(kFmt, 128, HD, false, true);
+    const uint32_t aQ = smem_u32(sQ), adO = smem_u32(sdO);
+    // S = Q K^T, dP = dO V^T: A is the 128-query tile, B the streamed key tile.
+    auto gemm_ss = [&](uint32_t d, uint32_t a_tile, uint32_t b_tile) {
 #pragma unroll
-        for (int ks = 0; ks < C::KSTEP_S; ++ks)
-          umma_ss<kKind>(d, kmajor_desc(a_tile, 128, ks), kmajor_desc(b_tile, KT, ks), idesc_s, ks > 0 ? 1u : 0u);
-      };
-      bool ok = mbar_wait_warp(q_full, 0, abort_flag, limit, 23) &&
-                mbar_wait_warp(&k_full[0], 0, abort_flag, limit, 24) &&
-                mbar_wait_warp(&v_full[0], 0, abort_flag, limit, 25);
-      if (ok) {
-        tc_fence_after();
-        if (elect_one()) {
-          gemm_ss(tbase + C::Q_S, aQ, smem_u32(sK(0)));
-          umma_commit(s_full);
-          gemm_ss(tbase + C::q_dp(0), adO, smem_u32(sV(0)));
-          umma_commit(&dp_full[0]);
-          umma_commit(&v_empty[0]);
-        }
-        __syncwarp();
+      for (int ks = 0; ks < C::KSTEP_S; ++ks)
+        umma_ss<kKind>(d, kmajor_desc(a_tile, 128, ks), kmajor_desc(b_tile, KT, ks), idesc_s, ks > 0 ? 1u : 0u);
+    };
+    // dQ (+)= dS K: A = dS from TMEM, B = the key tile read MN-major.
+    auto gemm_dq = [&](int st, bool acc) {
+      const uint32_t bK = smem_u32(sKm(st));
+#pragma unroll
+      for (int ks = 0; ks < KT / C::K_PER; ++ks)
+        umma_ts<kKind>(tbase + C::Q_DQ, tbase + C::q_dp(0) + C::a_col(ks, HALF),
+                       mnmajor_desc<C::TF32>(bK, KT, ks, C::K_PER), idesc_t, (acc || ks > 0) ? 1u : 0u);
+    };
+    int g = 0, ni = 0;
+    bool ok = true;
+    for (int r = 0; ok; ++r) {
+      const int w = snake_item(r, cta, G);
+      if (r * G >= n_items) break;
+      if (w >= n_items) continue;
+      int qt, bh;
+      const int n_kv = item(w, qt, bh);
+      if (n_kv == 0) continue;
+      if (!(ok = mbar_wait_warp(q_full, ni & 1, abort_flag, limit, 23))) break;
+      // first S of the item: the compute warps must have read the last one
+      if (g > 0 && !(ok = mbar_wait_warp(s_free, (g - 1) & 1, abort_flag, limit, 26))) break;
+      if (!(ok = mbar_wait_warp(&k_full[g % KST], (g / KST) & 1, abort_flag, limit, 24))) break;
+      tc_fence_after();
+      if (elect_one()) {
+        gemm_ss(tbase + C::Q_S, aQ, smem_u32(sK(g % KST)));
+        umma_commit(s_full);
       }
-      // Double-buffered: S and dP of key tile j+1 are queued before the dQ
-      // GEMM of tile j, which waits for the compute warps.
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int st = j % KST;
-        const int st1 = (j + 1) % KST;
-        const uint32_t ph1 = ((j + 1) / KST) & 1;
-        const int vst1 = (j + 1) % VST;
-        const uint32_t vph1 = ((j + 1) / VST) & 1;
-        const int b = C::Q_DBL ? (j & 1) : 0;
+      __syncwarp();
+      if (!(ok = mbar_wait_warp(&v_full[g % VST], (g / VST) & 1, abort_flag, limit, 25))) break;
+      tc_fence_after();
+      if (elect_one()) {
+        gemm_ss(tbase + C::q_dp(0), adO, smem_u32(sV(g % VST)));
+        umma_commit(dp_full);
+        umma_commit(&v_empty[g % VST]);
+        if (n_kv == 1) umma_commit(q_empty);
+      }
+      __syncwarp();
+      for (int j = 0; j < n_kv; ++j, ++g) {
+        const int st = g % KST;
         if (j + 1 < n_kv) {
-          if (!(ok = mbar_wait_warp(s_free, j & 1, abort_flag, limit, 26))) break;
-          if (!(ok = mbar_wait_warp(&k_full[st1], ph1, abort_flag, limit, 27))) break;
+          const int st1 = (g + 1) % KST;
+          if (!(ok = mbar_wait_warp(s_free, g & 1, abort_flag, limit, 26))) break;
+          if (!(ok = mbar_wait_warp(&k_full[st1], ((g + 1) / KST) & 1, abort_flag, limit, 27))) break;
           tc_fence_after();
           if (elect_one()) {
             gemm_ss(tbase + C::Q_S, aQ, smem_u32(sK(st1)));
             umma_commit(s_full);
           }
           __syncwarp();
-          if constexpr (C::Q_DBL) {
-            if (!(ok = mbar_wait_warp(&v_full[vst1], vph1, abort_flag, limit, 29))) break;
-            tc_fence_after();
-            if (elect_one()) {
-              gemm_ss(tbase + C::q_dp(b ^ 1), adO, smem_u32(sV(vst1)));
-              umma_commit(&dp_full[b ^ 1]);
-              umma_commit(&v_empty[vst1]);
-            }
-            __syncwarp();
-          }
         }
-        if (!(ok = mbar_wait_warp(&ds_full[b], C::Q_DBL ? ((j >> 1) & 1) : (j & 1), abort_flag, limit, 28))) break;
+        if (!(ok = mbar_wait_warp(ds_full, g & 1, abort_flag, limit, 28))) break;
+        // the accumulator is free once the previous item's epilogue read it
+        if (j == 0 && ni > 0 && !(ok = mbar_wait_warp(acc_free, (ni - 1) & 1, abort_flag, limit, 33))) break;
         tc_fence_after();
         if (elect_one()) {
-          const uint32_t bK = smem_u32(sKm(st));
-#pragma unroll
-          for (int ks = 0; ks < KT / C::K_PER; ++ks)
-            umma_ts<kKind>(tbase + C::Q_DQ, tbase + C::q_dp(b) + C::a_col(ks, HALF),
-                           mnmajor_desc<C::TF32>(bK, KT, ks, C::K_PER), idesc_t, (j > 0 || ks > 0) ? 1u : 0u);
+          gemm_dq(st, j > 0);
           umma_commit(&k_empty[st]);
         }
         __syncwarp();
         if (j + 1 < n_kv) {
-          if constexpr (!C::Q_DBL) {
-            if (!(ok = mbar_wait_warp(&v_full[vst1], vph1, abort_flag, limit, 29))) break;
-            tc_fence_after();
-            if (elect_one()) {
-              gemm_ss(tbase + C::q_dp(0), adO, smem_u32(sV(vst1)));
-              umma_commit(&dp_full[0]);
-              umma_commit(&v_empty[vst1]);
-            }
-            __syncwarp();
+          const int vst1 = (g + 1) % VST;
+          if (!(ok = mbar_wait_warp(&v_full[vst1], ((g + 1) / VST) & 1, abort_flag, limit, 29))) break;
+          tc_fence_after();
+          if (elect_one()) {
+            gemm_ss(tbase + C::q_dp(0), adO, smem_u32(sV(vst1)));
+            umma_commit(dp_full);
+            umma_commit(&v_empty[vst1]);
+            if (j + 2 == n_kv) umma_commit(q_empty);  // last GEMM reading Q / dO of this item
           }
+          __syncwarp();
         } else {
           if (elect_one()) umma_commit(acc_full);
           __syncwarp();
         }
       }
-      if (elect_one()) umma_commit(done_bar);
-      __syncwarp();
-      const uint64_t t0 = globaltimer_ns();
-      while (!mbar_try_wait(done_bar, 0) && globaltimer_ns() - t0 < limit) {
-      }
+      ++ni;
+    }
+    // Wait (bounded, regardless of abort) for every MMA issued so far, so
+    // that TMEM is idle before it is released.
+    if (elect_one()) umma_commit(done_bar);
+    __syncwarp();
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(done_bar, 0) && globaltimer_ns() - t0 < limit) {
     }
     __syncwarp();
-  } else {
+  } else if (warp < 8) {
     // --------------------------- compute warps ---------------------------
     const int h = threadIdx.x >> 7;   // key-column half
-    const int r = threadIdx.x & 127;  // query row (TMEM lane)
+    const int rr = threadIdx.x & 127;  // query row (TMEM lane)
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    const int q = qt * C::Q_ROWS + r;
-    const bool q_ok = q < p.Tq;
     const float sl2 = p.scale_log2;
     const float scale = p.scale;
-    const size_t lrow = (size_t)bh * p.q_rows_alloc + p.q_row0 + q;
-    const float L = q_ok ? p.lse2[(size_t)bh * p.Tq_pad + q] : 0.f;
-    const float dl = q_ok ? p.delta[(size_t)bh * p.Tq_pad + q] : 0.f;
-    int vis = p.Tk - 1;
-    if (p.causal) vis = min(vis, q + p.causal_offset);
-    if (!q_ok) vis = -1;
+    const int col = h * (HD / 2);
+    int g = 0, ni = 0;
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      const int b = C::Q_DBL ? (j & 1) : 0;
-      const uint32_t ph = C::Q_DBL ? ((j >> 1) & 1) : (j & 1);
-      const int kc0 = j * KT + h * HALF;  // first key of this thread's half
-      if (!(ok = mbar_wait(s_full, j & 1, abort_flag, limit, 30))) break;
-      float s[HALF];
-      float dsv[HALF];
-      if constexpr (C::Q_DBL) {
-        // S and dP of this tile were queued together: one TMEM round trip
-        if (!(ok = mbar_wait(&dp_full[b], ph, abort_flag, limit, 31))) break;
-        tc_fence_after();
-        tmem_load_row_async(tbase + lane_off + C::Q_S + h * HALF, s);
-        tmem_load_row_async(tbase + lane_off + C::q_dp(b) + h * HALF, dsv);
-        tmem_wait_ld();
-      } else {
-        tc_fence_after();
-        tmem_load_row(tbase + lane_off + C::Q_S + h * HALF, s);
-      }
-      tc_fence_before();
-      mbar_arrive(s_free);
-      const int lim = vis - kc0;  // columns > lim are masked (diagonal / tail tiles only)
+    for (int r = 0; ok; ++r) {
+      const int w = snake_item(r, cta, G);
+      if (r * G >= n_items) break;
+      if (w >= n_items) continue;
+      int qt, bh;
+      const int n_kv = item(w, qt, bh);
+      const int q = qt * C::Q_ROWS + rr;
+      const bool q_ok = q < p.Tq;
+      const size_t lrow = (size_t)bh * p.q_rows_alloc + p.q_row0 + q;
+      if (n_kv == 0) {  // no key visible to this query tile: dQ = 0
+        if (!p.accumulate && q_ok) {
+          uint32_t zero[HD / 2];
 #pragma unroll
-      for (int c = 0; c < HALF; ++c) s[c] = ex2_approx(fmaf(s[c], sl2, -L));
-      if (lim < HALF - 1) {
-#pragma unroll
-        for (int c = 0; c < HALF; ++c)
-          if (c > lim) s[c] = 0.f;
+          for (int i = 0; i < HD / 2; ++i) zero[i] = 0u;
+          row_store<DT, HD / 2>(zero, reinterpret_cast<DT*>(p.dq) + lrow * HD + col, false);
+        }
+        continue;
       }
-      if constexpr (!C::Q_DBL) {
-        if (!(ok = mbar_wait(&dp_full[b], ph, abort_flag, limit, 31))) break;
+      const float L = q_ok ? p.lse2[(size_t)bh * p.Tq_pad + q] : 0.f;
+      const float dl = q_ok ? p.delta[(size_t)bh * p.Tq_pad + q] : 0.f;
+      int vis = p.Tk - 1;
+      if (p.causal) vis = min(vis, q + p.causal_offset);
+      if (!q_ok) vis = -1;
+      for (int j = 0; j < n_kv; ++j, ++g) {
+        const int kc0 = j * KT + h * HALF;  // first key of this thread's half
+        if (!(ok = mbar_wait(s_full, g & 1, abort_flag, limit, 30))) break;
         tc_fence_after();
-        tmem_load_row(tbase + lane_off + C::q_dp(b) + h * HALF, dsv);
-      }
+        float sv[HALF];
+        tmem_load_row(tbase + lane_off + C::Q_S + h * HALF, sv);
+        tc_fence_before();
+        mbar_arrive(s_free);
+        const int lim = vis - kc0;  // columns > lim are masked (diagonal / tail tiles only)
 #pragma unroll
-      for (int c = 0; c < HALF; ++c) dsv[c] = s[c] * (dsv[c] - dl) * scale;
-      tmem_store_operand<DT>(tbase + lane_off + C::q_dp(b) + h * HALF, dsv);
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&ds_full[b]);
-    }
-    if (ok && n_kv > 0) ok = mbar_wait(acc_full, 0, abort_flag, limit, 32);
-    if (ok) {
+        for (int c = 0; c < HALF; ++c) sv[c] = ex2_approx(fmaf(sv[c], sl2, -L));
+        if (lim < HALF - 1) {
+#pragma unroll
+          for (int c = 0; c < HALF; ++c)
+            if (c > lim) sv[c] = 0.f;
+        }
+        if (!(ok = mbar_wait(dp_full, g & 1, abort_flag, limit, 31))) break;
+        tc_fence_after();
+        float dsv[HALF];
+        tmem_load_row(tbase + lane_off + C::q_dp(0) + h * HALF, dsv);
+#pragma unroll
+        for (int c = 0; c < HALF; ++c) dsv[c] = sv[c] * (dsv[c] - dl) * scale;
+        tmem_store_operand<DT>(tbase + lane_off + C::q_dp(0) + h * HALF, dsv);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(ds_full);
+      }
+      if (!ok) break;
+      // epilogue: accumulator -> registers, release it, then write the row
+      if (!(ok = mbar_wait(acc_full, ni & 1, abort_flag, limit, 32))) break;
       tc_fence_after();
-      const int col = h * (HD / 2);
-      if (p.accumulate) {
-        if (n_kv > 0)
-          tmem_row_accumulate<HD / 2>(tbase + lane_off + C::Q_DQ + col,
-                                      reinterpret_cast<float*>(p.dq) + lrow * HD + col, q_ok);
-      } else {
-        tmem_row_to_global<DT, HD / 2>(tbase + lane_off + C::Q_DQ + col,
-                                       reinterpret_cast<DT*>(p.dq) + lrow * HD + col, q_ok, n_kv == 0);
+      uint32_t acc[HD / 2];
+      tmem_row_load<HD / 2>(tbase + lane_off + C::Q_DQ + col, acc);
+      tc_fence_before();
+      mbar_arrive(acc_free);
+      if (q_ok) {
+        if (p.accumulate)
+          row_store<DT, HD / 2>(acc, reinterpret_cast<float*>(p.dq) + lrow * HD + col, true);
+        else
+          row_store<DT, HD / 2>(acc, reinterpret_cast<DT*>(p.dq) + lrow * HD + col, false);
       }
+      ++ni;
     }
   }
 

@@ -99,6 +99,15 @@ int device_is_sm100(bool* yes) {
   return CTFA_OK;
 }
 
+// Streaming multiprocessors of the current device (persistent grids).
+long long sm_count() {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+      sms <= 0)
+    return 148;
+  return sms;
+}
+
 // ---------------------------------------------------------------------------
 // Problem description shared by the full-sequence and block entry points.
 // ---------------------------------------------------------------------------
@@ -223,12 +232,10 @@ int launch_round(const void* const* in, void* const* out, int count, size_t elem
   }
   job.n4 = (long long)(elems / 4);
   job.count = count;
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long sms = sm_count();
   // one resident wave (8 blocks of 256 threads per SM) over all tensors
   const long long want = (job.n4 + 255) / 256;
-  dim3 grid((unsigned)std::max<long long>(1, std::min<long long>(want, ((long long)sms * 8 + count - 1) / count)), count);
+  dim3 grid((unsigned)std::max<long long>(1, std::min<long long>(want, (sms * 8 + count - 1) / count)), count);
   round_tf32_kernel<<<grid, 256, 0, stream>>>(job);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? CTFA_OK : cuda_fail(e, "launch round_tf32_kernel");
@@ -449,7 +456,10 @@ int launch_bwd_tc(const Problem& pr, const void* q, const void* k, const void* v
   auto kdq = attn_bwd_dq_sm100<DT, HD>;
   e = cudaFuncSetAttribute(kdq, cudaFuncAttributeMaxDynamicSharedMemorySize, C::Q_SMEM);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attn_bwd_dq_sm100)");
-  kdq<<<(unsigned)((long long)n_qt * BH), C::THREADS, C::Q_SMEM, stream>>>(q_q, q_k, q_v, q_do, q_km, p, n_qt);
+  // persistent: one CTA per SM (or per item when there are fewer items)
+  const long long dq_items = (long long)n_qt * BH;
+  const unsigned dq_grid = (unsigned)std::min<long long>(dq_items, sm_count());
+  kdq<<<dq_grid, C::THREADS, C::Q_SMEM, stream>>>(q_q, q_k, q_v, q_do, q_km, p, n_qt, (int)dq_items);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch attn_bwd_dq_sm100");
   record(ev, 3, stream);
