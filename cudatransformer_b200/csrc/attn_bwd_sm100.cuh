@@ -202,17 +202,14 @@ struct BwdConfig {
   static constexpr int Q_VST = TF32 ? 1 : Q_KST;
   // dK/dV kernel TMEM map (columns, lanes = keys).  One buffer holds dP^T,
   // then dS^T (tf32: in place, P^T in the next KV_QT columns; 16-bit: dS^T|P^T
-  // packed per half).  With KV_DBL the buffer is doubled so that the next dP^T
-  // GEMM is queued before the compute warps release the current one, and the
-  // compute warps read S^T and dP^T with one TMEM round trip (tf32 only).  Off:
-  // measured 4-8% slower.  Thread-side TMEM loads/stores take ~4x longer while
-  // the tensor pipe is busy, and the early dP^T puts them under a running MMA.
+  // packed per half).  A second buffer, so that the next dP^T GEMM is queued
+  // before the compute warps release the current one, measured 4-8% slower:
+  // thread-side TMEM loads/stores take ~4x longer while the tensor pipe is
+  // busy, and the early dP^T puts them under a running MMA.
   static constexpr int KV_HALF = KV_QT / 2;  // score columns per compute warpgroup
   static constexpr int KV_S = 0;
   static constexpr int KV_BUF = TF32 ? 2 * KV_QT : KV_QT;
-  static constexpr bool KV_DBL = false;
-  static constexpr int KV_NBUF = KV_DBL ? 2 : 1;
-  static constexpr int KV_DK = KV_QT + KV_NBUF * KV_BUF;
+  static constexpr int KV_DK = KV_QT + KV_BUF;
   static constexpr int KV_DV = KV_DK + HD;
   static constexpr uint32_t KV_TMEM = tmem_cols_for(KV_DV + HD);
   __host__ __device__ static constexpr int kv_dp(int b) { return KV_QT + b * KV_BUF; }
@@ -232,7 +229,6 @@ struct BwdConfig {
   static_assert(KV_ST >= 1 && Q_KST >= 1 && Q_VST >= 1, "shared memory budget");
   static_assert(Q_SMEM <= 232448, "dQ kernel shared memory");
   static_assert(KV_DV + HD <= 512 && Q_DQ + HD <= 512, "TMEM budget");
-  static_assert(!KV_DBL || KV_QT + 2 * KV_BUF + 2 * HD <= 512, "TMEM budget (double-buffered dP^T)");
   static_assert(HD * EB % 128 == 0, "head dim must fill whole 128-byte rows");
   static_assert(KV_HALF % 32 == 0 && Q_HALF % 32 == 0, "compute halves are whole 32-column TMEM loads");
 
@@ -252,16 +248,6 @@ __device__ __forceinline__ void tmem_load_row(uint32_t taddr, float (&v)[N]) {
 #pragma unroll
   for (int c = 0; c < N / 32; ++c) tmem_ld32f(taddr + c * 32, v + c * 32);
   tmem_wait_ld();
-}
-
-// Issue the loads of `N` fp32 TMEM columns into v[] without waiting for them
-// (tcgen05.wait::ld before use).  Thread-side TMEM accesses are slow while the
-// tensor pipe is busy (measured ~4x the idle latency), so loads that are ready
-// together are issued together and waited for once.
-template <int N>
-__device__ __forceinline__ void tmem_load_row_async(uint32_t taddr, float (&v)[N]) {
-#pragma unroll
-  for (int c = 0; c < N / 32; ++c) tmem_ld32f(taddr + c * 32, v + c * 32);
 }
 
 // Store v[] as an MMA A operand: tf32 (one column per value, rounded to
@@ -359,329 +345,6 @@ __device__ __forceinline__ void tmem_row_to_global(uint32_t taddr, DT* dst, bool
   }
 }
 
-// ---------------------------------------------------------------------------
-// dK / dV: one CTA per (128-key tile, batch*head)
-// ---------------------------------------------------------------------------
-template <typename DT, int HD>
-__global__ void __launch_bounds__(320, 1)
-    attn_bwd_dkdv_sm100(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                        const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                        const __grid_constant__ CUtensorMap tm_qm, const __grid_constant__ CUtensorMap tm_dom,
-                        const BwdParams p) {
-  using C = BwdConfig<DT, HD>;
-  constexpr int ST = C::KV_ST;
-  constexpr int QT = C::KV_QT;
-  constexpr int HALF = C::KV_HALF;
-  constexpr int kKind = DTypeTraits<DT>::kKind;
-  constexpr uint32_t kFmt = DTypeTraits<DT>::kFmt;
-  constexpr int TMA_WARP = 8, MMA_WARP = 9;
-
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sK = smem;
-  uint8_t* sV = sK + C::BIG_TILE;
-  uint8_t* sStage = sV + C::BIG_TILE;  // per stage: Q, dO [, Q MN copy, dO MN copy]
-  auto sQ = [&](int st) { return sStage + st * C::KV_STAGE_BYTES; };
-  auto sdO = [&](int st) { return sStage + st * C::KV_STAGE_BYTES + C::KV_QTILE; };
-  auto sQm = [&](int st) { return C::TF32 ? sStage + st * C::KV_STAGE_BYTES + 2 * C::KV_QTILE : sQ(st); };
-  auto sdOm = [&](int st) { return C::TF32 ? sStage + st * C::KV_STAGE_BYTES + 3 * C::KV_QTILE : sdO(st); };
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + ST * C::KV_STAGE_BYTES);
-  uint64_t* kv_full = bars;
-  uint64_t* q_full = kv_full + 1;   // [ST]
-  uint64_t* q_empty = q_full + ST;  // [ST]
-  uint64_t* s_full = q_empty + ST;
-  uint64_t* s_free = s_full + 1;
-  uint64_t* dp_full = s_free + 1;  // [2] per dP buffer
-  uint64_t* p_full = dp_full + 2;  // [2] per dP buffer
-  uint64_t* acc_full = p_full + 2;
-  uint64_t* done_bar = acc_full + 1;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done_bar + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int kt = (int)(blockIdx.x / p.BH);
-  const int bh = (int)(blockIdx.x % p.BH);
-  const int key0 = kt * C::KV_KEYS;
-
-  // Query tiles that see at least one key of this tile.
-  const int n_qt_all = (p.Tq + QT - 1) / QT;
-  int qt_first = 0;
-  if (p.causal) {
-    const int need = key0 - p.causal_offset;  // smallest query index that sees key0
-    qt_first = need <= 0 ? 0 : need / QT;
-  }
-  const int n_it = max(0, n_qt_all - qt_first);
-
-  if (threadIdx.x == 0) {
-    mbar_init(kv_full, 1);
-    for (int s = 0; s < ST; ++s) {
-      mbar_init(&q_full[s], 1);
-      mbar_init(&q_empty[s], 1);
-    }
-    mbar_init(s_full, 1);
-    mbar_init(s_free, 256);
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&dp_full[b], 1);
-      mbar_init(&p_full[b], 256);
-    }
-    mbar_init(acc_full, 1);
-    mbar_init(done_bar, 1);
-    *abort_flag = 0;
-    fence_barrier_init();
-  }
-  if (warp == MMA_WARP) {
-    tmem_alloc(tmem_holder, C::KV_TMEM);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tbase = *tmem_holder;
-  const uint64_t limit = p.wait_limit_ns;
-
-  if (warp == TMA_WARP) {
-    if (lane == 0 && n_it > 0) {
-      tma_prefetch_desc(&tm_q);
-      tma_prefetch_desc(&tm_k);
-      tma_prefetch_desc(&tm_v);
-      tma_prefetch_desc(&tm_do);
-      mbar_arrive_expect_tx(kv_full, 2 * C::BIG_TILE);
-#pragma unroll
-      for (int b = 0; b < C::KBLK; ++b) {
-        tma_load_3d(sK + b * 128 * 128, &tm_k, kv_full, b * C::E128, p.k_row0 + key0, bh);
-        tma_load_3d(sV + b * 128 * 128, &tm_v, kv_full, b * C::E128, p.k_row0 + key0, bh);
-      }
-      int issued = 0;
-      for (int it = 0; it < n_it; ++it) {
-        const int st = it % ST;
-        if (!mbar_wait(&q_empty[st], ((it / ST) & 1) ^ 1, abort_flag, limit, 11)) break;
-        const int row = p.q_row0 + (qt_first + it) * QT;
-        mbar_arrive_expect_tx(&q_full[st], C::KV_STAGE_BYTES);
-#pragma unroll
-        for (int b = 0; b < C::KBLK; ++b) {
-          tma_load_3d(sQ(st) + b * QT * 128, &tm_q, &q_full[st], b * C::E128, row, bh);
-          tma_load_3d(sdO(st) + b * QT * 128, &tm_do, &q_full[st], b * C::E128, row, bh);
-          if constexpr (C::TF32) {
-            tma_load_3d(sQm(st) + b * QT * 128, &tm_qm, &q_full[st], b * C::E128, row, bh);
-            tma_load_3d(sdOm(st) + b * QT * 128, &tm_dom, &q_full[st], b * C::E128, row, bh);
-          }
-        }
-        issued = it + 1;
-      }
-      if (*abort_flag) {
-        const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(kv_full, 0) && globaltimer_ns() - t0 < limit) {
-        }
-        for (int it = max(0, issued - ST); it < issued; ++it)
-          while (!mbar_try_wait(&q_full[it % ST], (it / ST) & 1) && globaltimer_ns() - t0 < limit) {
-          }
-      }
-    }
-    __syncwarp();
-  } else if (warp == MMA_WARP) {
-    // The whole warp runs this loop; one elected lane issues each MMA group.
-    if (n_it > 0) {
-      constexpr uint32_t idesc_s = make_idesc(kFmt, 128, QT, false, false);
-      constexpr uint32_t idesc_t = make_idesc(kFmt, 128, HD, false, true);
-      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV);
-      // S^T = K Q^T, dP^T = V dO^T: A is the 128-key tile, B the streamed query tile.
-      auto gemm_ss = [&](uint32_t d, uint32_t a_tile, uint32_t b_tile) {
-#pragma unroll
-        for (int ks = 0; ks < C::KSTEP_S; ++ks)
-          umma_ss<kKind>(d, kmajor_desc(a_tile, 128, ks), kmajor_desc(b_tile, QT, ks), idesc_s, ks > 0 ? 1u : 0u);
-      };
-      // dV += P^T dO, dK += dS^T Q: A from TMEM, B = MN-major query tile.
-      auto gemm_ts = [&](uint32_t d, uint32_t a_base, uint32_t b_tile, bool acc) {
-#pragma unroll
-        for (int ks = 0; ks < QT / C::K_PER; ++ks)
-          umma_ts<kKind>(d, a_base + C::a_col(ks, HALF), mnmajor_desc<C::TF32>(b_tile, QT, ks, C::K_PER), idesc_t,
-                         (acc || ks > 0) ? 1u : 0u);
-      };
-      bool ok = mbar_wait_warp(kv_full, 0, abort_flag, limit, 12) &&
-                mbar_wait_warp(&q_full[0], 0, abort_flag, limit, 13);
-      if (ok) {
-        tc_fence_after();
-        if (elect_one()) {
-          gemm_ss(tbase + C::KV_S, aK, smem_u32(sQ(0)));
-          umma_commit(s_full);
-          gemm_ss(tbase + C::kv_dp(0), aV, smem_u32(sdO(0)));
-          umma_commit(&dp_full[0]);
-        }
-        __syncwarp();
-      }
-      // Double-buffered: S^T and dP^T of tile it+1 are queued before the
-      // dV/dK GEMMs of tile it, which wait for the compute warps.
-      for (int it = 0; ok && it < n_it; ++it) {
-        const int st = it % ST;
-        const int st1 = (it + 1) % ST;
-        const int b = C::KV_DBL ? (it & 1) : 0;
-        if (it + 1 < n_it) {
-          if (!(ok = mbar_wait_warp(s_free, it & 1, abort_flag, limit, 14))) break;
-          if (!(ok = mbar_wait_warp(&q_full[st1], ((it + 1) / ST) & 1, abort_flag, limit, 15))) break;
-          tc_fence_after();
-          if (elect_one()) {
-            gemm_ss(tbase + C::KV_S, aK, smem_u32(sQ(st1)));
-            umma_commit(s_full);
-            if constexpr (C::KV_DBL) {
-              gemm_ss(tbase + C::kv_dp(b ^ 1), aV, smem_u32(sdO(st1)));
-              umma_commit(&dp_full[b ^ 1]);
-            }
-          }
-          __syncwarp();
-        }
-        if (!(ok = mbar_wait_warp(&p_full[b], C::KV_DBL ? ((it >> 1) & 1) : (it & 1), abort_flag, limit, 16))) break;
-        tc_fence_after();
-        if (elect_one()) {
-          gemm_ts(tbase + C::KV_DV, tbase + C::kv_p(b), smem_u32(sdOm(st)), it > 0);
-          gemm_ts(tbase + C::KV_DK, tbase + C::kv_dp(b), smem_u32(sQm(st)), it > 0);
-          umma_commit(&q_empty[st]);
-          if (it + 1 < n_it) {
-            if constexpr (!C::KV_DBL) {
-              gemm_ss(tbase + C::kv_dp(0), aV, smem_u32(sdO(st1)));
-              umma_commit(&dp_full[0]);
-            }
-          } else {
-            umma_commit(acc_full);
-          }
-        }
-        __syncwarp();
-      }
-      if (elect_one()) umma_commit(done_bar);
-      __syncwarp();
-      const uint64_t t0 = globaltimer_ns();
-      while (!mbar_try_wait(done_bar, 0) && globaltimer_ns() - t0 < limit) {
-      }
-    }
-    __syncwarp();
-  } else {
-    // --------------------------- compute warps ---------------------------
-    const int h = threadIdx.x >> 7;   // column half
-    const int r = threadIdx.x & 127;  // key row inside the tile (TMEM lane)
-    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    const int key = key0 + r;
-    const bool key_ok = key < p.Tk;
-    const float sl2 = p.scale_log2;
-    const float scale = p.scale;
-    // lse*log2(e) and delta for this head, padded to whole tiles (+inf / 0 on
-    // padding rows), 16-byte aligned: whole float4 loads, no bounds checks.
-    const float* lse2_bh = p.lse2 + (size_t)bh * p.Tq_pad;
-    const float* delta_bh = p.delta + (size_t)bh * p.Tq_pad;
-    bool ok = true;
-    for (int it = 0; it < n_it; ++it) {
-      const int b = C::KV_DBL ? (it & 1) : 0;
-      const uint32_t ph = C::KV_DBL ? ((it >> 1) & 1) : (it & 1);
-      const int qtile0 = (qt_first + it) * QT;
-      const int q0 = qtile0 + h * HALF;
-      float L[HALF];
-#pragma unroll
-      for (int c = 0; c < HALF / 4; ++c) {
-        const float4 v4 = __ldg(reinterpret_cast<const float4*>(lse2_bh + q0) + c);
-        L[4 * c] = v4.x;
-        L[4 * c + 1] = v4.y;
-        L[4 * c + 2] = v4.z;
-        L[4 * c + 3] = v4.w;
-      }
-      if (!(ok = mbar_wait(s_full, it & 1, abort_flag, limit, 17))) break;
-      float s[HALF];
-      // kBatch: S^T and dP^T were queued together (double-buffered dP^T) and
-      // fit the registers: read both with one TMEM round trip.
-      constexpr bool kBatch = C::KV_DBL && HALF == 32;
-      uint32_t dpre[32];
-      if constexpr (kBatch) {
-        if (!(ok = mbar_wait(&dp_full[b], ph, abort_flag, limit, 18))) break;
-        tc_fence_after();
-        tmem_load_row_async(tbase + lane_off + C::KV_S + h * HALF, s);
-        tmem_ld32(tbase + lane_off + C::kv_dp(b) + h * HALF, dpre);
-        tmem_wait_ld();
-      } else {
-        tc_fence_after();
-        tmem_load_row(tbase + lane_off + C::KV_S + h * HALF, s);
-      }
-      tc_fence_before();
-      mbar_arrive(s_free);
-      // P^T = exp2(S^T * scale*log2e - lse*log2e); padding queries have lse = +inf
-#pragma unroll
-      for (int c = 0; c < HALF; ++c) s[c] = ex2_approx(fmaf(s[c], sl2, -L[c]));
-      // causal diagonal tile / keys past Tk: zero the invisible entries
-      if (!key_ok) {
-#pragma unroll
-        for (int c = 0; c < HALF; ++c) s[c] = 0.f;
-      } else if (p.causal && key0 + C::KV_KEYS - 1 > qtile0 + p.causal_offset) {
-        const int cmin = key - p.causal_offset - q0;  // first visible column
-#pragma unroll
-        for (int c = 0; c < HALF; ++c)
-          if (c < cmin) s[c] = 0.f;
-      }
-      if constexpr (!kBatch) {
-        if (!(ok = mbar_wait(&dp_full[b], ph, abort_flag, limit, 18))) break;
-        tc_fence_after();
-      }
-      // dS^T = P^T (dP^T - delta) * scale, 32 columns at a time, written in
-      // place (tf32) or packed into the already-read front of the dP buffer.
-#pragma unroll
-      for (int ch = 0; ch < HALF / 32; ++ch) {
-        float dsv[32];
-        {
-          uint32_t regs[32];
-          if constexpr (kBatch) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) regs[i] = dpre[i];
-          } else {
-            tmem_ld32(tbase + lane_off + C::kv_dp(b) + h * HALF + ch * 32, regs);
-            tmem_wait_ld();
-          }
-#pragma unroll
-          for (int c4 = 0; c4 < 8; ++c4) {
-            const float4 d4 = __ldg(reinterpret_cast<const float4*>(delta_bh + q0 + ch * 32) + c4);
-            const float dd[4] = {d4.x, d4.y, d4.z, d4.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int i = 4 * c4 + e;
-              dsv[i] = s[ch * 32 + i] * (__uint_as_float(regs[i]) - dd[e]) * scale;
-            }
-          }
-        }
-        if constexpr (C::TF32)
-          tmem_store_operand<DT>(tbase + lane_off + C::kv_dp(b) + h * HALF + ch * 32, dsv);
-        else
-          tmem_store_operand<DT>(tbase + lane_off + C::kv_dp(b) + h * HALF + ch * 16, dsv);
-      }
-      tmem_store_operand<DT>(tbase + lane_off + C::kv_p(b) + h * HALF, s);
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&p_full[b]);
-    }
-    // ------------------------------ epilogue ------------------------------
-    if (ok && n_it > 0) ok = mbar_wait(acc_full, 0, abort_flag, limit, 19);
-    if (ok) {
-      tc_fence_after();
-      const size_t row_index = (size_t)bh * p.k_rows_alloc + p.k_row0 + key;
-      const int col = h * (HD / 2);
-      if (p.accumulate) {
-        if (n_it > 0) {
-          tmem_row_accumulate<HD / 2>(tbase + lane_off + C::KV_DK + col,
-                                      reinterpret_cast<float*>(p.dk) + row_index * HD + col, key_ok);
-          tmem_row_accumulate<HD / 2>(tbase + lane_off + C::KV_DV + col,
-                                      reinterpret_cast<float*>(p.dv) + row_index * HD + col, key_ok);
-        }
-      } else {
-        tmem_row_to_global<DT, HD / 2>(tbase + lane_off + C::KV_DK + col,
-                                       reinterpret_cast<DT*>(p.dk) + row_index * HD + col, key_ok, n_it == 0);
-        tmem_row_to_global<DT, HD / 2>(tbase + lane_off + C::KV_DV + col,
-                                       reinterpret_cast<DT*>(p.dv) + row_index * HD + col, key_ok, n_it == 0);
-      }
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == MMA_WARP) {
-    tc_fence_after();
-    tmem_dealloc(tbase, C::KV_TMEM);
-  }
-}
-
 // Load `COLS` fp32 TMEM columns of this thread's lane into registers (one
 // wait for all of them).
 template <int COLS>
@@ -733,6 +396,358 @@ __device__ __forceinline__ void row_store(const uint32_t (&r)[COLS], void* dst, 
 // rounds right to left.  With items sorted by decreasing cost this balances
 // persistent CTAs as well as dynamic scheduling does for these grids.
 __device__ __forceinline__ int snake_item(int r, int c, int G) { return r * G + ((r & 1) ? (G - 1 - c) : c); }
+
+// ---------------------------------------------------------------------------
+// dK / dV: persistent CTAs; each walks (128-key tile, batch*head) items, heavy
+// first.  K/V of the next item load once the current item's last S^T / dP^T
+// GEMMs ran; the next item's GEMMs overlap the current epilogue.
+// ---------------------------------------------------------------------------
+template <typename DT, int HD>
+__global__ void __launch_bounds__(320, 1)
+    attn_bwd_dkdv_sm100(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                        const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                        const __grid_constant__ CUtensorMap tm_qm, const __grid_constant__ CUtensorMap tm_dom,
+                        const BwdParams p, int n_ktiles, int n_items) {
+  using C = BwdConfig<DT, HD>;
+  constexpr int ST = C::KV_ST;
+  constexpr int QT = C::KV_QT;
+  constexpr int HALF = C::KV_HALF;
+  constexpr int kKind = DTypeTraits<DT>::kKind;
+  constexpr uint32_t kFmt = DTypeTraits<DT>::kFmt;
+  constexpr int TMA_WARP = 8, MMA_WARP = 9;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + C::BIG_TILE;
+  uint8_t* sStage = sV + C::BIG_TILE;  // per stage: Q, dO [, Q MN copy, dO MN copy]
+  auto sQ = [&](int st) { return sStage + st * C::KV_STAGE_BYTES; };
+  auto sdO = [&](int st) { return sStage + st * C::KV_STAGE_BYTES + C::KV_QTILE; };
+  auto sQm = [&](int st) { return C::TF32 ? sStage + st * C::KV_STAGE_BYTES + 2 * C::KV_QTILE : sQ(st); };
+  auto sdOm = [&](int st) { return C::TF32 ? sStage + st * C::KV_STAGE_BYTES + 3 * C::KV_QTILE : sdO(st); };
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + ST * C::KV_STAGE_BYTES);
+  uint64_t* kv_full = bars;
+  uint64_t* kv_empty = kv_full + 1;
+  uint64_t* q_full = kv_empty + 1;  // [ST]
+  uint64_t* q_empty = q_full + ST;  // [ST]
+  uint64_t* s_full = q_empty + ST;
+  uint64_t* s_free = s_full + 1;
+  uint64_t* dp_full = s_free + 1;
+  uint64_t* p_full = dp_full + 1;
+  uint64_t* acc_full = p_full + 1;
+  uint64_t* acc_free = acc_full + 1;
+  uint64_t* done_bar = acc_free + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int G = (int)gridDim.x, cta = (int)blockIdx.x;
+  const int n_qt_all = (p.Tq + QT - 1) / QT;
+  // item -> key tile, batch*head, first query tile that sees the key tile,
+  // number of query tiles (causal: heavy key tiles, i.e. low kt, first)
+  auto item = [&](int w, int& kt, int& bh, int& qt_first) -> int {
+    kt = w / p.BH;
+    bh = w % p.BH;
+    qt_first = 0;
+    if (p.causal) {
+      const int need = kt * C::KV_KEYS - p.causal_offset;  // smallest query index that sees the tile
+      qt_first = need <= 0 ? 0 : need / QT;
+    }
+    return max(0, n_qt_all - qt_first);
+  };
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(kv_empty, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&q_full[s], 1);
+      mbar_init(&q_empty[s], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 256);
+    mbar_init(dp_full, 1);
+    mbar_init(p_full, 256);
+    mbar_init(acc_full, 1);
+    mbar_init(acc_free, 256);
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == MMA_WARP) {
+    tmem_alloc(tmem_holder, C::KV_TMEM);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_holder;
+  const uint64_t limit = p.wait_limit_ns;
+  (void)n_ktiles;
+
+  if (warp == TMA_WARP) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      tma_prefetch_desc(&tm_do);
+      int g = 0, ni = 0;  // query tiles and non-empty items issued so far
+      int issued_kv = 0, issued = 0;
+      bool ok = true;
+      for (int r = 0; ok; ++r) {
+        const int w = snake_item(r, cta, G);
+        if (r * G >= n_items) break;
+        if (w >= n_items) continue;
+        int kt, bh, qt_first;
+        const int n_it = item(w, kt, bh, qt_first);
+        if (n_it == 0) continue;
+        // K/V buffers are free once the previous item's last S^T/dP^T ran
+        if (!(ok = mbar_wait(kv_empty, (ni & 1) ^ 1, abort_flag, limit, 10))) break;
+        const int krow = p.k_row0 + kt * C::KV_KEYS;
+        mbar_arrive_expect_tx(kv_full, 2 * C::BIG_TILE);
+#pragma unroll
+        for (int b = 0; b < C::KBLK; ++b) {
+          tma_load_3d(sK + b * 128 * 128, &tm_k, kv_full, b * C::E128, krow, bh);
+          tma_load_3d(sV + b * 128 * 128, &tm_v, kv_full, b * C::E128, krow, bh);
+        }
+        issued_kv = ni + 1;
+        for (int it = 0; it < n_it; ++it, ++g) {
+          const int st = g % ST;
+          if (!(ok = mbar_wait(&q_empty[st], ((g / ST) & 1) ^ 1, abort_flag, limit, 11))) break;
+          const int row = p.q_row0 + (qt_first + it) * QT;
+          mbar_arrive_expect_tx(&q_full[st], C::KV_STAGE_BYTES);
+#pragma unroll
+          for (int b = 0; b < C::KBLK; ++b) {
+            tma_load_3d(sQ(st) + b * QT * 128, &tm_q, &q_full[st], b * C::E128, row, bh);
+            tma_load_3d(sdO(st) + b * QT * 128, &tm_do, &q_full[st], b * C::E128, row, bh);
+            if constexpr (C::TF32) {
+              tma_load_3d(sQm(st) + b * QT * 128, &tm_qm, &q_full[st], b * C::E128, row, bh);
+              tma_load_3d(sdOm(st) + b * QT * 128, &tm_dom, &q_full[st], b * C::E128, row, bh);
+            }
+          }
+          issued = g + 1;
+        }
+        ++ni;
+      }
+      // On an aborted run some loads may still be landing: wait (bounded,
+      // ignoring the abort flag) for the last load issued into each buffer.
+      if (*abort_flag) {
+        const uint64_t t0 = globaltimer_ns();
+        if (issued_kv > 0)
+          while (!mbar_try_wait(kv_full, (issued_kv - 1) & 1) && globaltimer_ns() - t0 < limit) {
+          }
+        for (int it = max(0, issued - ST); it < issued; ++it)
+          while (!mbar_try_wait(&q_full[it % ST], (it / ST) & 1) && globaltimer_ns() - t0 < limit) {
+          }
+      }
+    }
+    __syncwarp();
+  } else if (warp == MMA_WARP) {
+    // The whole warp runs this loop; one elected lane issues each MMA group.
+    constexpr uint32_t idesc_s = make_idesc(kFmt, 128, QT, false, false);
+    constexpr uint32_t idesc_t = make_idesc(kFmt, 128, HD, false, true);
+    const uint32_t aK = smem_u32(sK), aV = smem_u32(sV);
+    // S^T = K Q^T, dP^T = V dO^T: A is the 128-key tile, B the streamed query tile.
+    auto gemm_ss = [&](uint32_t d, uint32_t a_tile, uint32_t b_tile) {
+#pragma unroll
+      for (int ks = 0; ks < C::KSTEP_S; ++ks)
+        umma_ss<kKind>(d, kmajor_desc(a_tile, 128, ks), kmajor_desc(b_tile, QT, ks), idesc_s, ks > 0 ? 1u : 0u);
+    };
+    // dV += P^T dO, dK += dS^T Q: A from TMEM, B = MN-major query tile.
+    auto gemm_ts = [&](uint32_t d, uint32_t a_base, uint32_t b_tile, bool acc) {
+#pragma unroll
+      for (int ks = 0; ks < QT / C::K_PER; ++ks)
+        umma_ts<kKind>(d, a_base + C::a_col(ks, HALF), mnmajor_desc<C::TF32>(b_tile, QT, ks, C::K_PER), idesc_t,
+                       (acc || ks > 0) ? 1u : 0u);
+    };
+    int g = 0, ni = 0;
+    bool ok = true;
+    for (int r = 0; ok; ++r) {
+      const int w = snake_item(r, cta, G);
+      if (r * G >= n_items) break;
+      if (w >= n_items) continue;
+      int kt, bh, qt_first;
+      const int n_it = item(w, kt, bh, qt_first);
+      if (n_it == 0) continue;
+      if (!(ok = mbar_wait_warp(kv_full, ni & 1, abort_flag, limit, 12))) break;
+      // first S^T of the item: the compute warps must have read the last one
+      if (g > 0 && !(ok = mbar_wait_warp(s_free, (g - 1) & 1, abort_flag, limit, 14))) break;
+      if (!(ok = mbar_wait_warp(&q_full[g % ST], (g / ST) & 1, abort_flag, limit, 13))) break;
+      tc_fence_after();
+      if (elect_one()) {
+        gemm_ss(tbase + C::KV_S, aK, smem_u32(sQ(g % ST)));
+        umma_commit(s_full);
+        gemm_ss(tbase + C::kv_dp(0), aV, smem_u32(sdO(g % ST)));
+        umma_commit(dp_full);
+        if (n_it == 1) umma_commit(kv_empty);
+      }
+      __syncwarp();
+      for (int it = 0; it < n_it; ++it, ++g) {
+        const int st = g % ST;
+        const int st1 = (g + 1) % ST;
+        if (it + 1 < n_it) {
+          if (!(ok = mbar_wait_warp(s_free, g & 1, abort_flag, limit, 14))) break;
+          if (!(ok = mbar_wait_warp(&q_full[st1], ((g + 1) / ST) & 1, abort_flag, limit, 15))) break;
+          tc_fence_after();
+          if (elect_one()) {
+            gemm_ss(tbase + C::KV_S, aK, smem_u32(sQ(st1)));
+            umma_commit(s_full);
+          }
+          __syncwarp();
+        }
+        if (!(ok = mbar_wait_warp(p_full, g & 1, abort_flag, limit, 16))) break;
+        // the accumulators are free once the previous item's epilogue read them
+        if (it == 0 && ni > 0 && !(ok = mbar_wait_warp(acc_free, (ni - 1) & 1, abort_flag, limit, 34))) break;
+        tc_fence_after();
+        if (elect_one()) {
+          gemm_ts(tbase + C::KV_DV, tbase + C::kv_p(0), smem_u32(sdOm(st)), it > 0);
+          gemm_ts(tbase + C::KV_DK, tbase + C::kv_dp(0), smem_u32(sQm(st)), it > 0);
+          umma_commit(&q_empty[st]);
+          if (it + 1 < n_it) {
+            gemm_ss(tbase + C::kv_dp(0), aV, smem_u32(sdO(st1)));
+            umma_commit(dp_full);
+            if (it + 2 == n_it) umma_commit(kv_empty);  // last GEMMs reading K / V of this item
+          } else {
+            umma_commit(acc_full);
+          }
+        }
+        __syncwarp();
+      }
+      ++ni;
+    }
+    // Wait (bounded, regardless of abort) for every MMA issued so far, so
+    // that TMEM is idle before it is released.
+    if (elect_one()) umma_commit(done_bar);
+    __syncwarp();
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(done_bar, 0) && globaltimer_ns() - t0 < limit) {
+    }
+    __syncwarp();
+  } else if (warp < 8) {
+    // --------------------------- compute warps ---------------------------
+    const int h = threadIdx.x >> 7;   // column half
+    const int rr = threadIdx.x & 127;  // key row inside the tile (TMEM lane)
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const float sl2 = p.scale_log2;
+    const float scale = p.scale;
+    const int col = h * (HD / 2);
+    int g = 0, ni = 0;
+    bool ok = true;
+    for (int r = 0; ok; ++r) {
+      const int w = snake_item(r, cta, G);
+      if (r * G >= n_items) break;
+      if (w >= n_items) continue;
+      int kt, bh, qt_first;
+      const int n_it = item(w, kt, bh, qt_first);
+      const int key0 = kt * C::KV_KEYS;
+      const int key = key0 + rr;
+      const bool key_ok = key < p.Tk;
+      const size_t row_index = (size_t)bh * p.k_rows_alloc + p.k_row0 + key;
+      if (n_it == 0) {  // no query sees this key tile: dK = dV = 0
+        if (!p.accumulate && key_ok) {
+          uint32_t zero[HD / 2];
+#pragma unroll
+          for (int i = 0; i < HD / 2; ++i) zero[i] = 0u;
+          row_store<DT, HD / 2>(zero, reinterpret_cast<DT*>(p.dk) + row_index * HD + col, false);
+          row_store<DT, HD / 2>(zero, reinterpret_cast<DT*>(p.dv) + row_index * HD + col, false);
+        }
+        continue;
+      }
+      // lse*log2(e) and delta for this head, padded to whole tiles (+inf / 0 on
+      // padding rows), 16-byte aligned: whole float4 loads, no bounds checks.
+      const float* lse2_bh = p.lse2 + (size_t)bh * p.Tq_pad;
+      const float* delta_bh = p.delta + (size_t)bh * p.Tq_pad;
+      for (int it = 0; it < n_it; ++it, ++g) {
+        const int qtile0 = (qt_first + it) * QT;
+        const int q0 = qtile0 + h * HALF;
+        float L[HALF];
+#pragma unroll
+        for (int c = 0; c < HALF / 4; ++c) {
+          const float4 v4 = __ldg(reinterpret_cast<const float4*>(lse2_bh + q0) + c);
+          L[4 * c] = v4.x;
+          L[4 * c + 1] = v4.y;
+          L[4 * c + 2] = v4.z;
+          L[4 * c + 3] = v4.w;
+        }
+        if (!(ok = mbar_wait(s_full, g & 1, abort_flag, limit, 17))) break;
+        tc_fence_after();
+        float sv[HALF];
+        tmem_load_row(tbase + lane_off + C::KV_S + h * HALF, sv);
+        tc_fence_before();
+        mbar_arrive(s_free);
+        // P^T = exp2(S^T * scale*log2e - lse*log2e); padding queries have lse = +inf
+#pragma unroll
+        for (int c = 0; c < HALF; ++c) sv[c] = ex2_approx(fmaf(sv[c], sl2, -L[c]));
+        // causal diagonal tile / keys past Tk: zero the invisible entries
+        if (!key_ok) {
+#pragma unroll
+          for (int c = 0; c < HALF; ++c) sv[c] = 0.f;
+        } else if (p.causal && key0 + C::KV_KEYS - 1 > qtile0 + p.causal_offset) {
+          const int cmin = key - p.causal_offset - q0;  // first visible column
+#pragma unroll
+          for (int c = 0; c < HALF; ++c)
+            if (c < cmin) sv[c] = 0.f;
+        }
+        if (!(ok = mbar_wait(dp_full, g & 1, abort_flag, limit, 18))) break;
+        tc_fence_after();
+        // dS^T = P^T (dP^T - delta) * scale, 32 columns at a time, written in
+        // place (tf32) or packed into the already-read front of the dP buffer.
+#pragma unroll
+        for (int ch = 0; ch < HALF / 32; ++ch) {
+          float dsv[32];
+          {
+            uint32_t regs[32];
+            tmem_ld32(tbase + lane_off + C::kv_dp(0) + h * HALF + ch * 32, regs);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c4 = 0; c4 < 8; ++c4) {
+              const float4 d4 = __ldg(reinterpret_cast<const float4*>(delta_bh + q0 + ch * 32) + c4);
+              const float dd[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int i = 4 * c4 + e;
+                dsv[i] = sv[ch * 32 + i] * (__uint_as_float(regs[i]) - dd[e]) * scale;
+              }
+            }
+          }
+          if constexpr (C::TF32)
+            tmem_store_operand<DT>(tbase + lane_off + C::kv_dp(0) + h * HALF + ch * 32, dsv);
+          else
+            tmem_store_operand<DT>(tbase + lane_off + C::kv_dp(0) + h * HALF + ch * 16, dsv);
+        }
+        tmem_store_operand<DT>(tbase + lane_off + C::kv_p(0) + h * HALF, sv);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(p_full);
+      }
+      if (!ok) break;
+      // ------------------------------ epilogue ------------------------------
+      if (!(ok = mbar_wait(acc_full, ni & 1, abort_flag, limit, 19))) break;
+      tc_fence_after();
+      if (p.accumulate) {
+        tmem_row_accumulate<HD / 2>(tbase + lane_off + C::KV_DK + col,
+                                    reinterpret_cast<float*>(p.dk) + row_index * HD + col, key_ok);
+        tmem_row_accumulate<HD / 2>(tbase + lane_off + C::KV_DV + col,
+                                    reinterpret_cast<float*>(p.dv) + row_index * HD + col, key_ok);
+      } else {
+        tmem_row_to_global<DT, HD / 2>(tbase + lane_off + C::KV_DK + col,
+                                       reinterpret_cast<DT*>(p.dk) + row_index * HD + col, key_ok, false);
+        tmem_row_to_global<DT, HD / 2>(tbase + lane_off + C::KV_DV + col,
+                                       reinterpret_cast<DT*>(p.dv) + row_index * HD + col, key_ok, false);
+      }
+      tc_fence_before();
+      mbar_arrive(acc_free);
+      ++ni;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == MMA_WARP) {
+    tc_fence_after();
+    tmem_dealloc(tbase, C::KV_TMEM);
+  }
+}
 
 // ---------------------------------------------------------------------------
 // dQ: persistent CTAs; each walks (128-query tile, batch*head) items, heavy

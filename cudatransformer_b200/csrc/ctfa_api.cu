@@ -448,8 +448,10 @@ int launch_bwd_tc(const Problem& pr, const void* q, const void* k, const void* v
   auto kdkdv = attn_bwd_dkdv_sm100<DT, HD>;
   e = cudaFuncSetAttribute(kdkdv, cudaFuncAttributeMaxDynamicSharedMemorySize, C::KV_SMEM);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attn_bwd_dkdv_sm100)");
-  kdkdv<<<(unsigned)((long long)n_kt * BH), C::THREADS, C::KV_SMEM, stream>>>(kv_q, kv_k, kv_v, kv_do, kv_qm,
-                                                                              kv_dom, p);
+  // persistent: one CTA per SM (or per item when there are fewer items)
+  const long long kv_items = (long long)n_kt * BH;
+  const unsigned kv_grid = (unsigned)std::min<long long>(kv_items, sm_count());
+  kdkdv<<<kv_grid, C::THREADS, C::KV_SMEM, stream>>>(kv_q, kv_k, kv_v, kv_do, kv_qm, kv_dom, p, n_kt, (int)kv_items);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch attn_bwd_dkdv_sm100");
   record(ev, 2, stream);
