@@ -15,8 +15,12 @@
 //                     S GEMM of tile j+1 needs K well before P V of tile j+1
 //                     needs V).
 //   warp  4*NQ+1    : tcgen05.mma issuer (one elected lane).
-//   warps 4*NQ+2,3  : spare (they complete the producer warpgroup, which hands
-//                     its registers to the softmax warpgroups via setmaxnreg).
+//   warps 4*NQ+2,3  : complete the producer warpgroup, which hands its
+//                     registers to the softmax warpgroups via setmaxnreg.  For
+//                     fp32 I/O (RND) they round every landed Q/K/V tile to tf32
+//                     (round to nearest) in shared memory before the MMAs read
+//                     it, and store the rounded tiles for the backward: Q by
+//                     every CTA, each K/V tile by one designated CTA.
 //
 //   V is the MN-major B operand of P V: 128B swizzle for 16-bit types, the
 //   32-byte-granule variant for tf32.
@@ -68,7 +72,7 @@ struct FwdConfig {
   static constexpr int KSTEP_PV = BN / K_PER_PV;
   static constexpr int P_COLS = (EB == 4) ? BN : BN / 2;
   static constexpr uint32_t TMEM_COLS = tmem_cols_for(NQ * (BN + HD));
-  static constexpr int NUM_BARS = 1 + 2 * KST + 2 * VST + 3 * NQ + 1;
+  static constexpr int NUM_BARS = 1 + 2 * KST + 2 * VST + 3 * NQ + 1 + (1 + KST + VST);
   static constexpr int SMEM_BYTES = 1024 + NQ * Q_TILE_BYTES + (KST + VST) * KV_TILE_BYTES + NUM_BARS * 8 + 16;
   // NQ softmax warpgroups + one producer warpgroup (TMA warp, MMA warp, two
   // spare warps) so that registers can be rebalanced per warpgroup.
@@ -85,11 +89,14 @@ struct FwdConfig {
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
 
-template <typename DT, int HD, int NQ, int BN, int KST, int VST>
+template <typename DT, int HD, int NQ, int BN, int KST, int VST, bool RND>
 __global__ void __launch_bounds__(NQ * 128 + 128, 1)
     attn_fwd_sm100(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                   const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
+                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_qr,
+                   const __grid_constant__ CUtensorMap tm_kr, const __grid_constant__ CUtensorMap tm_vr,
+                   const FwdParams p) {
   using C = FwdConfig<DT, HD, NQ, BN, KST, VST>;
+  static_assert(!RND || C::EB == 4, "in-kernel rounding is for fp32 I/O");
   constexpr int BM = C::BM;
   constexpr int kKind = DTypeTraits<DT>::kKind;
   constexpr uint32_t kFmt = DTypeTraits<DT>::kFmt;
@@ -111,7 +118,14 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
   uint64_t* p_full = s_full + NQ;
   uint64_t* o_full = p_full + NQ;
   uint64_t* done_bar = o_full + NQ;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done_bar + 1);
+  // RND: tiles rounded in shared memory (what the MMAs wait for instead of the TMA barriers)
+  uint64_t* q_ready = done_bar + 1;
+  uint64_t* k_ready = q_ready + 1;    // [KST]
+  uint64_t* v_ready = k_ready + KST;  // [VST]
+  uint64_t* q_go = RND ? q_ready : q_full;
+  uint64_t* k_go = RND ? k_ready : k_full;
+  uint64_t* v_go = RND ? v_ready : v_full;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(v_ready + VST);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -146,14 +160,19 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    // RND: a stage is empty once the MMAs read it and the rounding warps
+    // finished with it (their store of the rounded tile included)
     for (int s = 0; s < KST; ++s) {
       mbar_init(&k_full[s], 1);
-      mbar_init(&k_empty[s], 1);
+      mbar_init(&k_empty[s], RND ? 2 : 1);
+      mbar_init(&k_ready[s], 64);
     }
     for (int s = 0; s < VST; ++s) {
       mbar_init(&v_full[s], 1);
-      mbar_init(&v_empty[s], 1);
+      mbar_init(&v_empty[s], RND ? 2 : 1);
+      mbar_init(&v_ready[s], 64);
     }
+    mbar_init(q_ready, 64);
     for (int k = 0; k < NQ; ++k) {
       mbar_init(&s_full[k], 1);
       mbar_init(&p_full[k], 128);
@@ -261,8 +280,8 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
         }
       };
 
-      bool ok = mbar_wait_warp(q_full, 0, abort_flag, limit, 3);
-      if (ok) ok = mbar_wait_warp(&k_full[0], 0, abort_flag, limit, 4);
+      bool ok = mbar_wait_warp(q_go, 0, abort_flag, limit, 3);
+      if (ok) ok = mbar_wait_warp(&k_go[0], 0, abort_flag, limit, 4);
       if (ok) {
         tc_fence_after();
         if (elect_one()) {
@@ -280,7 +299,7 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
       for (int j = 0; ok && j < n_max; ++j) {
         const int st = j % VST;
         const int st1 = (j + 1) % KST;
-        if (!(ok = mbar_wait_warp(&v_full[st], (j / VST) & 1, abort_flag, limit, 5))) break;
+        if (!(ok = mbar_wait_warp(&v_go[st], (j / VST) & 1, abort_flag, limit, 5))) break;
         bool next_k = false;
 #pragma unroll
         for (int k = 0; k < NQ; ++k) {
@@ -294,7 +313,7 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
           __syncwarp();
           if (j + 1 < n_kv[k]) {
             if (!next_k) {
-              if (!(ok = mbar_wait_warp(&k_full[st1], ((j + 1) / KST) & 1, abort_flag, limit, 7))) break;
+              if (!(ok = mbar_wait_warp(&k_go[st1], ((j + 1) / KST) & 1, abort_flag, limit, 7))) break;
               tc_fence_after();
               next_k = true;
             }
@@ -320,7 +339,79 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
       }
     }
     __syncwarp();
-  }  // spare warps of the producer warpgroup have no role
+  } else if constexpr (RND) {
+    // ------------------ rounding warps (fp32 I/O, warps 4*NQ+2,3) ------------------
+    const int sub = (warp - MMA_WARP - 1) * 32 + lane;  // 0..63
+    const bool leader = (sub == 0);
+    // Round a landed tile in place and make the writes visible to the async
+    // proxy (tcgen05.mma, TMA store); the caller then arrives on the tile's
+    // ready barrier (64 arrivals), which the MMA warp and the storing lane wait on.
+    auto round_tile = [&](uint8_t* tile, int bytes) {
+      float4* t4 = reinterpret_cast<float4*>(tile);
+      for (int i = sub; i < bytes / 16; i += 64) {
+        float4 x = t4[i];
+        x.x = __uint_as_float(f32_to_tf32_rna(x.x));
+        x.y = __uint_as_float(f32_to_tf32_rna(x.y));
+        x.z = __uint_as_float(f32_to_tf32_rna(x.z));
+        x.w = __uint_as_float(f32_to_tf32_rna(x.w));
+        t4[i] = x;
+      }
+      fence_proxy_async_smem();
+    };
+    // K/V tile t of this head is stored by the one CTA whose query group
+    // contains key row t*BN (it loads the tile under the causal mask too).
+    auto designated = [&](int t) { return min((t * BN) / (NQ * BM), p.n_groups - 1) == group; };
+    bool ok = n_max > 0;
+    if (ok && (ok = mbar_wait(q_full, 0, abort_flag, limit, 42))) {
+#pragma unroll
+      for (int k = 0; k < NQ; ++k)
+        if (n_kv[k] > 0) round_tile(sQ + k * C::Q_TILE_BYTES, C::Q_TILE_BYTES);
+      mbar_arrive(q_ready);
+      if (leader && (ok = mbar_wait(q_ready, 0, abort_flag, limit, 45))) {
+#pragma unroll
+        for (int k = 0; k < NQ; ++k) {
+          if (n_kv[k] == 0) continue;
+          const int row = p.q_row0 + (group * NQ + k) * BM;
+#pragma unroll
+          for (int b = 0; b < C::KBLK; ++b)
+            tma_store_3d(&tm_qr, sQ + k * C::Q_TILE_BYTES + b * BM * 128, b * C::E128, row, bh);
+        }
+        tma_store_commit();
+      }
+    }
+    for (int t = 0; ok && t < n_max; ++t) {
+      const bool mine = designated(t);
+      const int kst = t % KST, vst = t % VST;
+      if (!(ok = mbar_wait(&k_full[kst], (t / KST) & 1, abort_flag, limit, 43))) break;
+      round_tile(sK + kst * C::KV_TILE_BYTES, C::KV_TILE_BYTES);
+      mbar_arrive(&k_ready[kst]);
+      if (leader) {
+        if (mine && (ok = mbar_wait(&k_ready[kst], (t / KST) & 1, abort_flag, limit, 46))) {
+#pragma unroll
+          for (int b = 0; b < C::KBLK; ++b)
+            tma_store_3d(&tm_kr, sK + kst * C::KV_TILE_BYTES + b * BN * 128, b * C::E128, p.k_row0 + t * BN, bh);
+          tma_store_commit();
+          tma_store_wait_read();
+        }
+        mbar_arrive(&k_empty[kst]);
+      }
+      if (!(ok = mbar_wait(&v_full[vst], (t / VST) & 1, abort_flag, limit, 44))) break;
+      round_tile(sV + vst * C::KV_TILE_BYTES, C::KV_TILE_BYTES);
+      mbar_arrive(&v_ready[vst]);
+      if (leader) {
+        if (mine && (ok = mbar_wait(&v_ready[vst], (t / VST) & 1, abort_flag, limit, 47))) {
+#pragma unroll
+          for (int b = 0; b < C::KBLK; ++b)
+            tma_store_3d(&tm_vr, sV + vst * C::KV_TILE_BYTES + b * BN * 128, b * C::E128, p.k_row0 + t * BN, bh);
+          tma_store_commit();
+          tma_store_wait_read();
+        }
+        mbar_arrive(&v_empty[vst]);
+      }
+    }
+    if (leader) tma_store_wait_all();
+    __syncwarp();
+  }  // without RND the two remaining warps of the producer warpgroup have no role
   } else {
     // ---------------------------- softmax warps ----------------------------
     if constexpr (C::REBALANCE) regs_increase<C::SOFTMAX_REGS>();

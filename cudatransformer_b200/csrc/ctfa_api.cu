@@ -127,15 +127,27 @@ bool tensor_core_shape(const Problem& pr) {
          (pr.D == 64 || pr.D == 128);
 }
 
-template <typename DT, int HD, int NQ, int BN, int KST, int VST>
+// RND (fp32 I/O): q, k, v are the caller's fp32 tensors; the kernel rounds
+// every tile to tf32 in shared memory and writes the rounded copies to
+// rounded[0..2] (same layout) for the backward.
+template <typename DT, int HD, int NQ, int BN, int KST, int VST, bool RND = false>
 int launch_fwd_tc(const Problem& pr, const void* q, const void* k, const void* v, void* o, float* lse,
-                  cudaStream_t stream) {
+                  cudaStream_t stream, void* const* rounded = nullptr) {
   using C = FwdConfig<DT, HD, NQ, BN, KST, VST>;
-  CUtensorMap mq, mk, mv;
+  CUtensorMap mq, mk, mv, mqr, mkr, mvr;
   int s;
   if ((s = make_map(&mq, q, pr.dtype, HD, pr.q_rows, pr.B * pr.H, 128)) != CTFA_OK) return s;
   if ((s = make_map(&mk, k, pr.dtype, HD, pr.k_rows, pr.B * pr.H, BN)) != CTFA_OK) return s;
   if ((s = make_map(&mv, v, pr.dtype, HD, pr.k_rows, pr.B * pr.H, BN, sizeof(DT) == 4)) != CTFA_OK) return s;
+  if constexpr (RND) {
+    if ((s = make_map(&mqr, rounded[0], pr.dtype, HD, pr.q_rows, pr.B * pr.H, 128)) != CTFA_OK) return s;
+    if ((s = make_map(&mkr, rounded[1], pr.dtype, HD, pr.k_rows, pr.B * pr.H, BN)) != CTFA_OK) return s;
+    if ((s = make_map(&mvr, rounded[2], pr.dtype, HD, pr.k_rows, pr.B * pr.H, BN, true)) != CTFA_OK) return s;
+  } else {
+    mqr = mq;
+    mkr = mk;
+    mvr = mv;
+  }
   FwdParams p;
   p.BH = pr.B * pr.H;
   p.Tq = pr.Tq;
@@ -152,12 +164,12 @@ int launch_fwd_tc(const Problem& pr, const void* q, const void* k, const void* v
   p.o_f32 = pr.o_f32;
   p.lse = lse;
   p.wait_limit_ns = g_wait_limit_ns;
-  auto kern = attn_fwd_sm100<DT, HD, NQ, BN, KST, VST>;
+  auto kern = attn_fwd_sm100<DT, HD, NQ, BN, KST, VST, RND>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attn_fwd_sm100)");
   const long long grid = (long long)p.n_groups * p.BH;
   if (grid > 0x7fffffffLL) return fail(CTFA_ERR_UNSUPPORTED, "grid too large");
-  kern<<<(unsigned)grid, C::THREADS, C::SMEM_BYTES, stream>>>(mq, mk, mv, p);
+  kern<<<(unsigned)grid, C::THREADS, C::SMEM_BYTES, stream>>>(mq, mk, mv, mqr, mkr, mvr, p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch attn_fwd_sm100");
   return CTFA_OK;
@@ -274,10 +286,10 @@ int forward_impl(const Problem& pr, const void* q, const void* k, const void* v,
         const size_t n = (size_t)pr.B * pr.H * pr.q_rows * pr.D;
         char* w = reinterpret_cast<char*>(ws);
         void* r[3] = {w, w + align256(n * 4), w + 2 * align256(n * 4)};
-        const void* in[3] = {q, k, v};
-        if ((s = launch_round(in, r, 3, n, stream)) != CTFA_OK) return s;
-        return pr.D == 64 ? launch_fwd_tc<float, 64, 2, 128, 3, 2>(pr, r[0], r[1], r[2], o, lse, stream)
-                          : launch_fwd_tc<float, 128, 1, 64, 3, 2>(pr, r[0], r[1], r[2], o, lse, stream);
+        // rounding to tf32 happens inside the kernel, which also writes the
+        // rounded copies the backward reads (CTFA_DTYPE_TF32)
+        return pr.D == 64 ? launch_fwd_tc<float, 64, 2, 128, 3, 2, true>(pr, q, k, v, o, lse, stream, r)
+                          : launch_fwd_tc<float, 128, 1, 64, 3, 2, true>(pr, q, k, v, o, lse, stream, r);
       }
       case CTFA_DTYPE_TF32:
         return pr.D == 64 ? launch_fwd_tc<float, 64, 2, 128, 3, 2>(pr, q, k, v, o, lse, stream)

@@ -174,3 +174,28 @@ def test_fp32_backward_reuses_forward_rounding(cuda_device, ctfa):
         assert torch.equal(a, b)
     q.add_(0)  # bumps the version counter: the cache no longer matches
     layer.computeBackward(q, k, v, do)
+
+
+@pytest.mark.parametrize("T,D,causal", [(700, 64, True), (700, 64, False), (513, 128, True), (1024, 64, True)])
+def test_fp32_forward_writes_exact_rounded_copies(cuda_device, ctfa, T, D, causal):
+    """The fp32 forward rounds q/k/v to tf32 inside the kernel and stores the
+    rounded tiles (Q by every CTA, each K/V tile by one designated CTA) into
+    its workspace for the backward: every element must equal the
+    round-to-nearest-away tf32 value of the input, with no tile missing."""
+    from cudatransformer_b200 import _lib
+
+    B, H = 2, 3
+    q, k, v = (torch.randn(B, H, T, D, device=cuda_device) for _ in range(3))
+    o = torch.empty_like(q)
+    lse = torch.empty(B, H, T, device=cuda_device)
+    n = ctfa.ctfa_forward_workspace_bytes(B, H, T, D, _lib.CTFA_DTYPE_F32)
+    ws = torch.full((n,), 0x7F, dtype=torch.uint8, device=cuda_device)  # NaN-like poison
+    _lib.check(ctfa.ctfa_forward(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(), B, H, T, D,
+                                 _lib.CTFA_DTYPE_F32, int(causal), ws.data_ptr(), n,
+                                 torch.cuda.current_stream().cuda_stream), "ctfa_forward")
+    torch.cuda.synchronize()
+    a = (B * H * T * D * 4 + 255) // 256 * 256
+    for i, x in enumerate((q, k, v)):
+        got = ws[i * a:i * a + x.numel() * 4].view(torch.int32).view(B, H, T, D)
+        want = (x.contiguous().view(torch.int32) + 0x1000) & ~0x1FFF
+        assert torch.equal(got, want), f"rounded copy {i} differs"
