@@ -53,6 +53,11 @@ WORKLOADS = {
                     causal=True, qkv_scale=1.0, do_scale=0.1, seed=2),
     "config5": dict(desc="BASELINE config 5: long context, bf16, sequence sharded over the GPUs (ring)", B=1, H=32,
                     T=131072, D=128, dtype="bf16", causal=True, qkv_scale=1.0, do_scale=1.0, seed=4),
+    "config4": dict(desc="BASELINE config 4: NanoGPT training step (6 layers, d=384, 6 heads x 64, T=256, vocab 65, "
+                         "batch 64, fp32, Adam lr 3e-4)", B=64, H=6, T=256, D=64, dtype="f32", causal=False,
+                    layers=6, vocab=65, mlp=1536, lr=3e-4, seed=3),
+    "config4causal": dict(desc="BASELINE config 4 with the causal mask (language-model semantics)", B=64, H=6, T=256,
+                          D=64, dtype="f32", causal=True, layers=6, vocab=65, mlp=1536, lr=3e-4, seed=3),
 }
 
 
@@ -605,6 +610,171 @@ def run_reference(args, w):
     print(json.dumps(out), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# config 4: NanoGPT training step around this repository's attention
+# ---------------------------------------------------------------------------
+def run_config4(args, w):
+    """The reference NanoGPT architecture (token + position embedding, 6 blocks
+    of LayerNorm -> attention -> LayerNorm -> ReLU MLP with no residuals,
+    unembedding, softmax, cross-entropy on the probabilities, the reference's
+    Adam) with every attention forward/backward through cudatransformer_b200
+    and the rest as PyTorch ops (plumbing), fp32.  A step = forward, backward
+    and one Adam update on a fresh batch; steps are stateful, so the warm-up
+    steps are part of the training run and the loss of every step is kept.
+
+    Reported: step time, the share of it spent in attention (the same
+    attention work timed alone with CUDA events), and the loss of each step
+    against an fp64 restatement of the same model and optimizer
+    (oracle/nanogpt_oracle.py) fed the same weights and tokens.  The
+    reference's own NanoGPT is not run: its position embedding reads and
+    writes past its table for batch > 1 and its AttentionLayer backward
+    divides by zero (F3)."""
+    import numpy as np
+    import torch
+
+    from cudatransformer_b200 import FlashAttentionLayer
+    from cudatransformer_b200.autograd import flash_attention
+    from oracle import nanogpt_oracle as nano
+
+    rank, world, local = dist_init(args.gpus)
+    if rank != 0:
+        return
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    B, H, T, D, L, V, E = w["B"], w["H"], w["T"], w["D"], w["layers"], w["vocab"], w["H"] * w["D"]
+
+    # parameters named as the reference's NanoGPT.getParameters() names them
+    shapes = {"tokenEmbedding": (V, E), "positionEmbedding": (T, E), "unEmbedding": (V, E)}
+    for i in range(L):
+        for n in ("firstNorm", "secondNorm"):
+            shapes[f"layer_{i}.{n}.weights"] = (E,)
+            shapes[f"layer_{i}.{n}.biases"] = (E,)
+        for n in ("query", "key", "value", "output"):
+            shapes[f"layer_{i}.attention.{n}.weights"] = (E, E)
+            shapes[f"layer_{i}.attention.{n}.biases"] = (E,)
+        shapes[f"layer_{i}.mlp.layer_0.weights"] = (w["mlp"], E)
+        shapes[f"layer_{i}.mlp.layer_0.biases"] = (w["mlp"],)
+        shapes[f"layer_{i}.mlp.layer_2.weights"] = (E, w["mlp"])
+        shapes[f"layer_{i}.mlp.layer_2.biases"] = (E,)
+    rng = np.random.default_rng(w["seed"])
+    init = {}
+    for name in sorted(shapes):
+        if name.endswith("Norm.weights"):
+            init[name] = np.ones(shapes[name], dtype=np.float32)
+        elif name.endswith("biases"):
+            init[name] = np.zeros(shapes[name], dtype=np.float32)
+        else:
+            init[name] = (rng.standard_normal(shapes[name]) * 0.02).astype(np.float32)
+    n_steps = args.warmup + args.steps
+    brng = np.random.default_rng(w["seed"] + 1000)
+    data = []
+    for _ in range(n_steps):
+        ids = brng.integers(0, V, size=(B, T + 1), dtype=np.int64)
+        data.append((ids[:, :-1].copy(), ids[:, 1:].copy()))
+
+    def model(params, ids):
+        x = params["tokenEmbedding"][ids] + params["positionEmbedding"][:T].unsqueeze(0)
+        for i in range(L):
+            p = lambda n: params[f"layer_{i}.{n}"]
+            h = torch.nn.functional.layer_norm(x, (E,), p("firstNorm.weights"), p("firstNorm.biases"), 1e-5)
+            split = lambda t: t.view(B, T, H, D).transpose(1, 2).contiguous()
+            q = split(h @ p("attention.query.weights") + p("attention.query.biases"))
+            k = split(h @ p("attention.key.weights") + p("attention.key.biases"))
+            v = split(h @ p("attention.value.weights") + p("attention.value.biases"))
+            o = flash_attention(q, k, v, w["causal"]).transpose(1, 2).reshape(B, T, E)
+            a = o @ p("attention.output.weights") + p("attention.output.biases")
+            h2 = torch.nn.functional.layer_norm(a, (E,), p("secondNorm.weights"), p("secondNorm.biases"), 1e-5)
+            m = torch.relu(h2 @ p("mlp.layer_0.weights").T + p("mlp.layer_0.biases"))
+            x = m @ p("mlp.layer_2.weights").T + p("mlp.layer_2.biases")
+        return torch.softmax(x @ params["unEmbedding"].T, -1)
+
+    params = {k: torch.tensor(v, device=dev).requires_grad_() for k, v in init.items()}
+    opt = nano.ReferenceAdam(params, lr=w["lr"])
+    losses, times = [], []
+    with ClockSampler(local) as clocks:
+        for ids_np, tgt_np in data:
+            s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            s_ev.record()
+            ids = torch.as_tensor(ids_np, device=dev)
+            tgt = torch.as_tensor(tgt_np, device=dev)
+            for p_ in params.values():
+                p_.grad = None
+            loss = nano.loss_from_probs(model(params, ids), tgt)
+            loss.backward()
+            opt.step({k: p_.grad for k, p_ in params.items()})
+            lval = float(loss.detach())  # device -> host read of the step's loss
+            e_ev.record()
+            torch.cuda.synchronize()
+            times.append(s_ev.elapsed_time(e_ev))
+            losses.append(lval)
+    timed = times[args.warmup:]
+    ms = float(np.median(timed))
+
+    # attention alone: per layer one forward (saving states) and one backward
+    q, k, v, do = (torch.randn(B, H, T, D, device=dev) for _ in range(4))
+    att = FlashAttentionLayer(D, H, causal=w["causal"])
+
+    def att_unit():
+        for _ in range(L):
+            att.computeAttention(q, k, v, saveStates=True)
+            att.computeBackward(q, k, v, do)
+            att.clearCache()
+
+    for _ in range(3):
+        att_unit()
+    torch.cuda.synchronize()
+    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s_ev.record()
+    for _ in range(10):
+        att_unit()
+    e_ev.record()
+    torch.cuda.synchronize()
+    att_ms = s_ev.elapsed_time(e_ev) / 10
+
+    # fp64 restatement of the same training run (loss oracle), on the GPU for
+    # the full run; one step of it timed on the host cores as the CPU baseline
+    t0 = time.perf_counter()
+    ref_losses = nano.train(init, data, L, H, D, causal=w["causal"], lr=w["lr"], device=str(dev))
+    ref_seconds = time.perf_counter() - t0
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    t0 = time.perf_counter()
+    nano.train(init, data[:1], L, H, D, causal=w["causal"], lr=w["lr"], device="cpu")
+    cpu_step = time.perf_counter() - t0
+    diffs = [abs(a - b) for a, b in zip(losses, ref_losses)]
+    tokens = B * T
+    out = {
+        "metric": "NanoGPT training step time and attention share (config 4)",
+        "value": round(tokens / (ms * 1e-3), 1),
+        "unit": "tokens/s",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 3),
+        "higher_is_better": True,
+        "dtype": "fp32 I/O; attention on tf32 tcgen05 MMA, the rest PyTorch fp32",
+        "data": "synthetic: weights N(0,0.02) (LayerNorm scale 1, biases 0), token ids uniform [0,65), seeded",
+        "config": {"workload": w["desc"], "batch": B, "seq_len": T, "layers": L, "heads": H, "head_dim": D,
+                   "causal": w["causal"],
+                   "note": "causal (language-model mask)" if w["causal"] else "non-causal, as the reference's attention"},
+        "attention_ms_per_step": round(att_ms, 3),
+        "attention_share_of_step": round(att_ms / ms, 4),
+        "losses": [round(x, 6) for x in losses],
+        "restatement_fp64_losses": [round(x, 6) for x in ref_losses],
+        "max_abs_loss_diff_vs_restatement": round(max(diffs), 6),
+        "restatement": {"device": str(dev), "seconds": round(ref_seconds, 2),
+                        "source": "oracle/nanogpt_oracle.py (fp64, PyTorch)"},
+        "cpu_baseline": {"value": round(tokens / cpu_step, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": "one training step of the fp64 restatement on the host cores"},
+        "reference": {"unavailable": "the reference NanoGPT reads/writes past its position-embedding table for "
+                                     "batch > 1 (embedding_kernels.cu:64-76) and its AttentionLayer backward divides "
+                                     "by zero (F3); not run"},
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(out), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -616,7 +786,9 @@ def main():
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     w = WORKLOADS[args.workload]
-    if args.impl == "reference":
+    if args.workload in ("config4", "config4causal"):
+        run_config4(args, w)
+    elif args.impl == "reference":
         run_reference(args, w)
     else:
         run_ours(args, w)
