@@ -200,20 +200,23 @@ struct BwdConfig {
   static constexpr int Q_PAIR = (Q_BUDGET - 2 * BIG_TILE) / (Q_KSTAGE_BYTES + Q_VSTAGE_BYTES);
   static constexpr int Q_KST = TF32 ? 2 : (Q_PAIR > 3 ? 3 : Q_PAIR);
   static constexpr int Q_VST = TF32 ? 1 : Q_KST;
-  // dK/dV kernel TMEM map (columns, lanes = keys).  One buffer holds dP^T,
-  // then dS^T (tf32: in place, P^T in the next KV_QT columns; 16-bit: dS^T|P^T
-  // packed per half).  A second buffer, so that the next dP^T GEMM is queued
-  // before the compute warps release the current one, measured 4-8% slower:
-  // thread-side TMEM loads/stores take ~4x longer while the tensor pipe is
-  // busy, and the early dP^T puts them under a running MMA.
+  // dK/dV kernel TMEM map (columns, lanes = keys).  S^T, then the dP^T buffer
+  // (dS^T after the compute pass: tf32 in place; 16-bit: dS^T|P^T packed per
+  // half), then for tf32 two P^T buffers (EARLY_P: the compute warps store P^T
+  // right after the exponentials and release it, so dV (+)= P^T dO runs while
+  // they form dS^T; only dK waits for dS^T), then the dK and dV accumulators.
+  // A second dP^T buffer (so the next dP^T GEMM is queued before the compute
+  // warps release the current one) measured 4-8% slower: thread-side TMEM
+  // loads/stores take ~4x longer while the tensor pipe is busy.
   static constexpr int KV_HALF = KV_QT / 2;  // score columns per compute warpgroup
+  static constexpr bool EARLY_P = TF32;
   static constexpr int KV_S = 0;
-  static constexpr int KV_BUF = TF32 ? 2 * KV_QT : KV_QT;
-  static constexpr int KV_DK = KV_QT + KV_BUF;
+  static constexpr int KV_DP = KV_QT;
+  static constexpr int KV_DK = TF32 ? 4 * KV_QT : 2 * KV_QT;
   static constexpr int KV_DV = KV_DK + HD;
   static constexpr uint32_t KV_TMEM = tmem_cols_for(KV_DV + HD);
-  __host__ __device__ static constexpr int kv_dp(int b) { return KV_QT + b * KV_BUF; }
-  __host__ __device__ static constexpr int kv_p(int b) { return TF32 ? kv_dp(b) + KV_QT : kv_dp(b) + KV_HALF / 2; }
+  // P^T of tile g: tf32 buffer g % 2; 16-bit: packed into the dP^T buffer
+  __host__ __device__ static constexpr int kv_p(int b) { return TF32 ? 2 * KV_QT + b * KV_QT : KV_DP + KV_HALF / 2; }
   // dQ kernel TMEM map (lanes = queries): S, then a dP buffer (dS after the
   // compute pass: tf32 in place, 16-bit packed per half), then the dQ
   // accumulator.
@@ -433,8 +436,9 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* s_full = q_empty + ST;
   uint64_t* s_free = s_full + 1;
   uint64_t* dp_full = s_free + 1;
-  uint64_t* p_full = dp_full + 1;
-  uint64_t* acc_full = p_full + 1;
+  uint64_t* p_full = dp_full + 1;   // dS^T (and 16-bit P^T) stored
+  uint64_t* pt_full = p_full + 1;   // EARLY_P: P^T stored
+  uint64_t* acc_full = pt_full + 1;
   uint64_t* acc_free = acc_full + 1;
   uint64_t* done_bar = acc_free + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done_bar + 1);
@@ -468,6 +472,7 @@ __global__ void __launch_bounds__(320, 1)
     mbar_init(s_free, 256);
     mbar_init(dp_full, 1);
     mbar_init(p_full, 256);
+    mbar_init(pt_full, 256);
     mbar_init(acc_full, 1);
     mbar_init(acc_free, 256);
     mbar_init(done_bar, 1);
@@ -577,7 +582,7 @@ __global__ void __launch_bounds__(320, 1)
       if (elect_one()) {
         gemm_ss(tbase + C::KV_S, aK, smem_u32(sQ(g % ST)));
         umma_commit(s_full);
-        gemm_ss(tbase + C::kv_dp(0), aV, smem_u32(sdO(g % ST)));
+        gemm_ss(tbase + C::KV_DP, aV, smem_u32(sdO(g % ST)));
         umma_commit(dp_full);
         if (n_it == 1) umma_commit(kv_empty);
       }
@@ -595,16 +600,25 @@ __global__ void __launch_bounds__(320, 1)
           }
           __syncwarp();
         }
+        if constexpr (C::EARLY_P) {
+          // dV (+)= P^T dO as soon as P^T is stored, while dS^T is formed
+          if (!(ok = mbar_wait_warp(pt_full, g & 1, abort_flag, limit, 37))) break;
+          // the accumulators are free once the previous item's epilogue read them
+          if (it == 0 && ni > 0 && !(ok = mbar_wait_warp(acc_free, (ni - 1) & 1, abort_flag, limit, 34))) break;
+          tc_fence_after();
+          if (elect_one()) gemm_ts(tbase + C::KV_DV, tbase + C::kv_p(g & 1), smem_u32(sdOm(st)), it > 0);
+          __syncwarp();
+        }
         if (!(ok = mbar_wait_warp(p_full, g & 1, abort_flag, limit, 16))) break;
-        // the accumulators are free once the previous item's epilogue read them
-        if (it == 0 && ni > 0 && !(ok = mbar_wait_warp(acc_free, (ni - 1) & 1, abort_flag, limit, 34))) break;
+        if (!C::EARLY_P && it == 0 && ni > 0 && !(ok = mbar_wait_warp(acc_free, (ni - 1) & 1, abort_flag, limit, 34)))
+          break;
         tc_fence_after();
         if (elect_one()) {
-          gemm_ts(tbase + C::KV_DV, tbase + C::kv_p(0), smem_u32(sdOm(st)), it > 0);
-          gemm_ts(tbase + C::KV_DK, tbase + C::kv_dp(0), smem_u32(sQm(st)), it > 0);
+          if constexpr (!C::EARLY_P) gemm_ts(tbase + C::KV_DV, tbase + C::kv_p(0), smem_u32(sdOm(st)), it > 0);
+          gemm_ts(tbase + C::KV_DK, tbase + C::KV_DP, smem_u32(sQm(st)), it > 0);
           umma_commit(&q_empty[st]);
           if (it + 1 < n_it) {
-            gemm_ss(tbase + C::kv_dp(0), aV, smem_u32(sdO(st1)));
+            gemm_ss(tbase + C::KV_DP, aV, smem_u32(sdO(st1)));
             umma_commit(dp_full);
             if (it + 2 == n_it) umma_commit(kv_empty);  // last GEMMs reading K / V of this item
           } else {
@@ -688,6 +702,14 @@ __global__ void __launch_bounds__(320, 1)
           for (int c = 0; c < HALF; ++c)
             if (c < cmin) sv[c] = 0.f;
         }
+        if constexpr (C::EARLY_P) {
+          // P^T (buffer g % 2: dV of tile g-2, its last reader, completed
+          // before S^T of this tile, which the s_full wait above covered)
+          tmem_store_operand<DT>(tbase + lane_off + C::kv_p(g & 1) + h * HALF, sv);
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(pt_full);
+        }
         if (!(ok = mbar_wait(dp_full, g & 1, abort_flag, limit, 18))) break;
         tc_fence_after();
         // dS^T = P^T (dP^T - delta) * scale, 32 columns at a time, written in
@@ -697,7 +719,7 @@ __global__ void __launch_bounds__(320, 1)
           float dsv[32];
           {
             uint32_t regs[32];
-            tmem_ld32(tbase + lane_off + C::kv_dp(0) + h * HALF + ch * 32, regs);
+            tmem_ld32(tbase + lane_off + C::KV_DP + h * HALF + ch * 32, regs);
             tmem_wait_ld();
 #pragma unroll
             for (int c4 = 0; c4 < 8; ++c4) {
@@ -711,11 +733,11 @@ __global__ void __launch_bounds__(320, 1)
             }
           }
           if constexpr (C::TF32)
-            tmem_store_operand<DT>(tbase + lane_off + C::kv_dp(0) + h * HALF + ch * 32, dsv);
+            tmem_store_operand<DT>(tbase + lane_off + C::KV_DP + h * HALF + ch * 32, dsv);
           else
-            tmem_store_operand<DT>(tbase + lane_off + C::kv_dp(0) + h * HALF + ch * 16, dsv);
+            tmem_store_operand<DT>(tbase + lane_off + C::KV_DP + h * HALF + ch * 16, dsv);
         }
-        tmem_store_operand<DT>(tbase + lane_off + C::kv_p(0) + h * HALF, sv);
+        if constexpr (!C::EARLY_P) tmem_store_operand<DT>(tbase + lane_off + C::kv_p(0) + h * HALF, sv);
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(p_full);
