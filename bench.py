@@ -723,11 +723,11 @@ def run_config4(args, w):
             p = lambda n: params[f"layer_{i}.{n}"]
             h = torch.nn.functional.layer_norm(x, (E,), p("firstNorm.weights"), p("firstNorm.biases"), 1e-5)
             split = lambda t: t.view(B, T, H, D).transpose(1, 2).contiguous()
-            q = split(h @ p("attention.query.weights") + p("attention.query.biases"))
-            k = split(h @ p("attention.key.weights") + p("attention.key.biases"))
-            v = split(h @ p("attention.value.weights") + p("attention.value.biases"))
+            q = split(nano.project(h, p("attention.query.weights"), p("attention.query.biases")))
+            k = split(nano.project(h, p("attention.key.weights"), p("attention.key.biases")))
+            v = split(nano.project(h, p("attention.value.weights"), p("attention.value.biases")))
             o = flash_attention(q, k, v, w["causal"]).transpose(1, 2).reshape(B, T, E)
-            a = o @ p("attention.output.weights") + p("attention.output.biases")
+            a = nano.project(o, p("attention.output.weights"), p("attention.output.biases"))
             h2 = torch.nn.functional.layer_norm(a, (E,), p("secondNorm.weights"), p("secondNorm.biases"), 1e-5)
             m = torch.relu(h2 @ p("mlp.layer_0.weights").T + p("mlp.layer_0.biases"))
             x = m @ p("mlp.layer_2.weights").T + p("mlp.layer_2.biases")

@@ -6,5 +6,6 @@ reference's operator interface and the multi-GPU drivers.
 """
 from . import _lib
 from .flash_attention_layer import FlashAttentionLayer
+from .projection_layers import OutputProjectionLayer, QKVProjectionLayer
 
-__all__ = ["FlashAttentionLayer", "_lib"]
+__all__ = ["FlashAttentionLayer", "QKVProjectionLayer", "OutputProjectionLayer", "_lib"]

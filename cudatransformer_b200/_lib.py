@@ -67,6 +67,10 @@ SIGNATURES = {
     "ctfa_set_wait_limit_ns": (_c_int, [_c_ull]),
     "ctfa_check_device_error": (_c_int, [_c_void_p]),
     "ctfa_selftest_wait_timeout": (_c_int, [_c_ull, _c_void_p]),
+    "ctfa_qkv_forward": (_c_int, [_c_void_p] * 10 + [_c_int] * 6 + [_c_void_p]),
+    "ctfa_qkv_backward": (_c_int, [_c_void_p] * 14 + [_c_int] * 6 + [_c_void_p]),
+    "ctfa_out_proj_forward": (_c_int, [_c_void_p] * 4 + [_c_int] * 6 + [_c_void_p]),
+    "ctfa_out_proj_backward": (_c_int, [_c_void_p] * 6 + [_c_int] * 6 + [_c_void_p]),
 }
 
 _lib = None

@@ -838,3 +838,5 @@ extern "C" int ctfa_selftest_wait_timeout(unsigned long long limit_ns, void* str
   if (e != cudaSuccess) return cuda_fail(e, "launch selftest_wait_kernel");
   return ctfa_check_device_error(stream);
 }
+
+#include "proj_api.cuh"

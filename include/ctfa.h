@@ -192,6 +192,54 @@ int ctfa_check_device_error(void* stream);
  */
 int ctfa_selftest_wait_timeout(unsigned long long limit_ns, void* stream);
 
+/*
+ * Projections either side of the attention (the QKV projection and the output
+ * projection of cuda_transformer/AttentionLayer.cu), as tcgen05 GEMMs that read
+ * and write the head layout [B, H, T, D] directly.
+ *   x, y, dx, dy : [B, T, E]   (E = the layer's inputDim; rows of the model)
+ *   q, k, v, a, dq, dk, dv, da : [B, H, T, D]
+ *   wq, wk, wv   : H*D rows of E  (row n = output feature n; the buffer the
+ *                  reference's kernels index as W[n * inputDim + i],
+ *                  attention_qkv_kernels.cu:92)
+ *   wo           : E rows of H*D  (row o = output feature o,
+ *                  attention_proj_kernels.cu:83)
+ *   bq, bk, bv   : [H*D];  bo : [E]
+ * Element types as for the attention (CTFA_DTYPE_*).  f32 / bf16 / f16 with
+ * D = 64 or 128, 16-byte-aligned tensors and E * element size a multiple of 16
+ * bytes run on the tensor cores (fp32 operands as tf32: the tensor core reads
+ * their upper 19 bits; fp32 accumulation); other shapes and double run SIMT
+ * kernels.  Nothing is allocated or synchronised.
+ */
+/* q|k|v = x W^T + b, written as [B, H, T, D].  Replaces getQKVmatrices
+ * (QKVProjectionLayer::computeQKV, QKVProjectionLayer.cu:73-96).  Biases may
+ * be NULL (zero). */
+int ctfa_qkv_forward(const void* x, const void* wq, const void* bq, const void* wk, const void* bk, const void* wv,
+                     const void* bv, void* q, void* k, void* v, int B, int T, int E, int H, int D, int dtype,
+                     void* stream);
+/* Backward of the QKV projection.  Replaces qkvBackwardWB + qkvBackward
+ * (QKVProjectionLayer::computeBackward, QKVProjectionLayer.cu:100-141):
+ *   dw{q,k,v} += dq|dk|dv^T x, db{q,k,v} += column sums of dq|dk|dv (ADDED into
+ *   the buffers, like the reference's atomic accumulation);
+ *   dx = sum over q, k, v of d{q,k,v} W{q,k,v} (overwritten).
+ * dx == NULL skips the input gradient; dwq == dwk == dwv == NULL and the
+ * bias-gradient pointers NULL skip the parameter gradients (a bias-gradient
+ * pointer alone may be NULL). */
+int ctfa_qkv_backward(const void* x, const void* dq, const void* dk, const void* dv, const void* wq, const void* wk,
+                      const void* wv, void* dwq, void* dbq, void* dwk, void* dbk, void* dwv, void* dbv, void* dx,
+                      int B, int T, int E, int H, int D, int dtype, void* stream);
+/* y = a Wo^T + bo, a read as [B, H, T, D] with the heads concatenated per row.
+ * Replaces attentionProj (OutputProjectionLayer::forward,
+ * OutputProjectionLayer.cu:52-66).  bo may be NULL. */
+int ctfa_out_proj_forward(const void* a, const void* wo, const void* bo, void* y, int B, int T, int E, int H, int D,
+                          int dtype, void* stream);
+/* Backward of the output projection.  Replaces projBackwardWB + projBackward
+ * (OutputProjectionLayer::backward, OutputProjectionLayer.cu:69-97):
+ *   dwo += dy^T a, dbo += column sums of dy (added); da = dy Wo as
+ *   [B, H, T, D] (overwritten).  da == NULL or dwo == dbo == NULL skip the
+ *   respective part. */
+int ctfa_out_proj_backward(const void* a, const void* dy, const void* wo, void* dwo, void* dbo, void* da, int B,
+                           int T, int E, int H, int D, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -11,10 +11,12 @@ Restated from the reference sources (no code copied):
   -> MLP (Linear, ReLU, Linear), with NO residual connections;
 * LayerNorm, layer_norm_kernels.cu:34-90: biased variance, eps 1e-5, affine;
 * Linear, LinearLayer.cu:13,111: y = x W^T + b, W [out, in];
-* attention: q/k/v = x W + b with W [in, H*D] (QKVProjectionLayer.cu:16),
+* attention: q/k/v = x W^T + b, the weight buffer read as [H*D, in] (row =
+  output feature, attention_qkv_kernels.cu:92-95; getParameters labels it
+  [in, H*D], AttentionLayer.cu:342, which only matters when in != H*D),
   heads split as [B, T, H, D] -> [B, H, T, D]; softmax(q k^T / sqrt(D)) v
   (non-causal, as the reference's kernel; causal optional); output
-  projection a W_o + b_o with W_o [H*D, in] (OutputProjectionLayer.cu:14);
+  projection a W_o^T + b_o, W_o read as [in, H*D] (attention_proj_kernels.cu:83);
 * loss, loss_kernels.cu:150-189: mean over all B*T tokens of -log p[target],
   taken on the softmax *probabilities*;
 * Adam, adam_kernels.cu:44-52 and AdamOptimizer.cu:74-96: the bias-corrected
@@ -35,6 +37,13 @@ def layer_norm(x, w, b, eps=1e-5):
     return (x - mean) / torch.sqrt(var + eps) * w + b
 
 
+def project(x, w, b):
+    """x W^T + b with the weight buffer read row = output feature, whatever
+    shape label it carries (the reference's projection kernels index it as
+    [out, in])."""
+    return x @ w.reshape(-1, x.shape[-1]).T + b
+
+
 def attention_f64(q, k, v, causal: bool):
     s = (q @ k.transpose(-1, -2)) / math.sqrt(q.shape[-1])
     if causal:
@@ -53,11 +62,11 @@ def forward(params: dict, ids: torch.Tensor, num_layers: int, num_heads: int, he
         p = lambda name: params[f"layer_{i}.{name}"]
         h = layer_norm(x, p("firstNorm.weights"), p("firstNorm.biases"))
         split = lambda t: t.view(B, T, num_heads, head_dim).transpose(1, 2).contiguous()
-        q = split(h @ p("attention.query.weights") + p("attention.query.biases"))
-        k = split(h @ p("attention.key.weights") + p("attention.key.biases"))
-        v = split(h @ p("attention.value.weights") + p("attention.value.biases"))
+        q = split(project(h, p("attention.query.weights"), p("attention.query.biases")))
+        k = split(project(h, p("attention.key.weights"), p("attention.key.biases")))
+        v = split(project(h, p("attention.value.weights"), p("attention.value.biases")))
         o = attention(q, k, v, causal).transpose(1, 2).reshape(B, T, num_heads * head_dim)
-        a = o @ p("attention.output.weights") + p("attention.output.biases")
+        a = project(o, p("attention.output.weights"), p("attention.output.biases"))
         h2 = layer_norm(a, p("secondNorm.weights"), p("secondNorm.biases"))
         m = torch.relu(h2 @ p("mlp.layer_0.weights").T + p("mlp.layer_0.biases"))
         x = m @ p("mlp.layer_2.weights").T + p("mlp.layer_2.biases")

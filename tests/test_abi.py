@@ -79,3 +79,46 @@ def test_wait_limit_validation(ctfa):
     assert ctfa.ctfa_set_wait_limit_ns(0) == _lib.CTFA_ERR_INVALID_ARGUMENT
     assert ctfa.ctfa_set_wait_limit_ns(2_000_000_000) == _lib.CTFA_OK
     assert ctfa.ctfa_selftest_wait_timeout(0, None) == _lib.CTFA_ERR_INVALID_ARGUMENT
+
+
+def test_projection_argument_validation(ctfa):
+    """The projection entry points reject null tensors, non-positive sizes,
+    unknown dtypes and inconsistent gradient requests before any CUDA call."""
+    E = _lib.CTFA_ERR_INVALID_ARGUMENT
+    fwd = [FAKE] * 10 + [2, 16, 64, 1, 64, _lib.CTFA_DTYPE_F32, None]
+    for i in (0, 1, 3, 5, 7, 8, 9):  # x, wq, wk, wv, q, k, v are required (biases are optional)
+        a = list(fwd)
+        a[i] = None
+        assert ctfa.ctfa_qkv_forward(*a) == E
+    for i, bad in ((10, 0), (11, -1), (12, 0), (13, 0), (14, 0), (15, 9)):
+        a = list(fwd)
+        a[i] = bad
+        assert ctfa.ctfa_qkv_forward(*a) == E
+    bwd = [FAKE] * 14 + [2, 16, 64, 1, 64, _lib.CTFA_DTYPE_F32, None]
+    a = list(bwd)
+    a[1] = None  # dq
+    assert ctfa.ctfa_qkv_backward(*a) == E
+    a = list(bwd)
+    a[9] = None  # dwk missing while dwq, dwv given
+    assert ctfa.ctfa_qkv_backward(*a) == E
+    a = list(bwd)
+    a[0] = None  # x needed for the weight gradients
+    assert ctfa.ctfa_qkv_backward(*a) == E
+    a = list(bwd)
+    a[4] = None  # wq needed for dx
+    assert ctfa.ctfa_qkv_backward(*a) == E
+    ofwd = [FAKE] * 4 + [2, 16, 64, 1, 64, _lib.CTFA_DTYPE_BF16, None]
+    for i in (0, 1, 3):
+        a = list(ofwd)
+        a[i] = None
+        assert ctfa.ctfa_out_proj_forward(*a) == E
+    obwd = [FAKE] * 6 + [2, 16, 64, 1, 64, _lib.CTFA_DTYPE_BF16, None]
+    a = list(obwd)
+    a[1] = None  # dy
+    assert ctfa.ctfa_out_proj_backward(*a) == E
+    a = list(obwd)
+    a[0] = None  # a needed for dWo
+    assert ctfa.ctfa_out_proj_backward(*a) == E
+    a = list(obwd)
+    a[2] = None  # wo needed for da
+    assert ctfa.ctfa_out_proj_backward(*a) == E

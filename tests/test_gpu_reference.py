@@ -54,3 +54,61 @@ def test_library_matches_reference_cuda_on_o_and_dq(cuda_device):
     ours = run_library(q, k, v, do, "f32", False, cuda_device)
     assert orc.max_rel_err(ours["o"], ref["o"]) < TOL["f32"]
     assert orc.max_rel_err(ours["dq"], ref["dq"]) < TOL["f32"]
+
+
+@needs_ref
+def test_reference_projection_layers_match_oracle_and_library(cuda_device):
+    """The reference's own QKVProjectionLayer / OutputProjectionLayer (fp32
+    SIMT kernels) == the float64 restatement (pins its weight orientation and
+    accumulation), and libctfa_b200.so's tcgen05 projections == the reference
+    within the fp32 tolerance."""
+    import ctypes
+
+    from cudatransformer_b200 import projection_layers as pl
+    from oracle import projection_oracle as po
+
+    if not hasattr(REF, "ctref_qkv_projection"):
+        pytest.skip("libctref.so predates the projection entry points; rebuild with make -C oracle ref")
+    B, T, E, H, D = 2, 96, 192, 2, 64  # E != H*D: a transposed weight read would show
+    rng = np.random.default_rng(21)
+    mk = lambda *s, scale=1.0: torch.tensor(rng.standard_normal(s) * scale, dtype=torch.float32, device=cuda_device)
+    x = mk(B, T, E)
+    w = [mk(H * D, E, scale=E ** -0.5) for _ in range(3)]
+    b = [mk(H * D, scale=0.1) for _ in range(3)]
+    g = [mk(B, H, T, D) for _ in range(3)]
+    a, wo, bo, dy = mk(B, H, T, D), mk(E, H * D, scale=(H * D) ** -0.5), mk(E, scale=0.1), mk(B, T, E)
+    P3 = ctypes.c_void_p * 3
+    ptrs = lambda ts: P3(*(t.data_ptr() for t in ts))
+    out = [torch.empty(B, H, T, D, device=cuda_device) for _ in range(3)]
+    dx = torch.empty(B, T, E, device=cuda_device)
+    dw = [torch.empty(H * D, E, device=cuda_device) for _ in range(3)]
+    db = [torch.empty(H * D, device=cuda_device) for _ in range(3)]
+    rc = REF.ctref_qkv_projection(x.data_ptr(), ptrs(w), ptrs(b), ptrs(out), ptrs(g), dx.data_ptr(), ptrs(dw),
+                                  ptrs(db), B, T, E, H, D)
+    assert rc == 0
+    y = torch.empty(B, T, E, device=cuda_device)
+    da, dwo, dbo = torch.empty(B, H, T, D, device=cuda_device), torch.empty(E, H * D, device=cuda_device), torch.empty(
+        E, device=cuda_device)
+    rc = REF.ctref_out_projection(a.data_ptr(), wo.data_ptr(), bo.data_ptr(), y.data_ptr(), dy.data_ptr(),
+                                  da.data_ptr(), dwo.data_ptr(), dbo.data_ptr(), B, T, E, H, D)
+    assert rc == 0
+    n = lambda t: t.double().cpu().numpy()
+    oq = po.qkv_forward(n(x), n(w[0]), n(b[0]), n(w[1]), n(b[1]), n(w[2]), n(b[2]), H, D)
+    odx, odw, odb = po.qkv_backward(n(x), *(n(t) for t in g), *(n(t) for t in w))
+    oy = po.out_proj_forward(n(a), n(wo), n(bo))
+    oda, odwo, odbo = po.out_proj_backward(n(a), n(dy), n(wo))
+    # reference (fp32 SIMT) vs the restatement
+    for got, want in [*zip(out, oq), (dx, odx), *zip(dw, odw), *zip(db, odb), (y, oy), (da, oda), (dwo, odwo),
+                      (dbo, odbo)]:
+        assert po.max_rel_err(n(got), want) < 1e-5
+    # library (tf32 tensor cores) vs the reference
+    lq = pl.qkv_forward(x, w[0], b[0], w[1], b[1], w[2], b[2], H, D)
+    ldw = [torch.zeros_like(t) for t in w]
+    ldb = [torch.zeros_like(t) for t in b]
+    ldx = pl.qkv_backward(x, *g, *w, ldw[0], ldb[0], ldw[1], ldb[1], ldw[2], ldb[2])
+    ly = pl.out_proj_forward(a, wo, bo)
+    ldwo, ldbo = torch.zeros_like(wo), torch.zeros_like(bo)
+    lda = pl.out_proj_backward(a, dy, wo, ldwo, ldbo)
+    for got, want in [*zip(lq, out), (ldx, dx), *zip(ldw, dw), *zip(ldb, db), (ly, y), (lda, da), (ldwo, dwo),
+                      (ldbo, dbo)]:
+        assert po.max_rel_err(n(got), n(want)) < TOL["f32"]
