@@ -662,24 +662,25 @@ def run_config4(args, w):
     """The reference NanoGPT architecture (token + position embedding, 6 blocks
     of LayerNorm -> attention -> LayerNorm -> ReLU MLP with no residuals,
     unembedding, softmax, cross-entropy on the probabilities, the reference's
-    Adam) with every attention forward/backward through cudatransformer_b200
-    and the rest as PyTorch ops (plumbing), fp32.  A step = forward, backward
-    and one Adam update on a fresh batch; steps are stateful, so the warm-up
-    steps are part of the training run and the loss of every step is kept.
+    Adam) from cudatransformer_b200.nanogpt: the QKV projection, attention and
+    output projection of every block run on this library's tcgen05 kernels,
+    the rest as PyTorch ops (plumbing), fp32.  A step = forward, backward and
+    one Adam update on a fresh batch; steps are stateful, so the warm-up steps
+    are part of the training run and the loss of every step is kept.
 
-    Reported: step time, the share of it spent in attention (the same
-    attention work timed alone with CUDA events), and the loss of each step
-    against an fp64 restatement of the same model and optimizer
-    (oracle/nanogpt_oracle.py) fed the same weights and tokens.  The
-    reference's own NanoGPT is not run: its position embedding reads and
+    Reported: step time; the share of it spent in attention and in the two
+    projections (the same work timed alone with CUDA events); and the loss of
+    each step against an fp64 restatement of the same model and optimizer
+    (oracle/nanogpt_oracle.py, the checker) fed the same weights and tokens.
+    The reference's own NanoGPT is not run: its position embedding reads and
     writes past its table for batch > 1 and its AttentionLayer backward
     divides by zero (F3)."""
     import numpy as np
     import torch
 
     from cudatransformer_b200 import FlashAttentionLayer
-    from cudatransformer_b200.autograd import flash_attention
-    from oracle import nanogpt_oracle as nano
+    from cudatransformer_b200 import nanogpt as model
+    from cudatransformer_b200 import projection_layers as pl
 
     rank, world, local = dist_init(args.gpus)
     if rank != 0:
@@ -688,28 +689,7 @@ def run_config4(args, w):
     torch.cuda.set_device(dev)
     B, H, T, D, L, V, E = w["B"], w["H"], w["T"], w["D"], w["layers"], w["vocab"], w["H"] * w["D"]
 
-    # parameters named as the reference's NanoGPT.getParameters() names them
-    shapes = {"tokenEmbedding": (V, E), "positionEmbedding": (T, E), "unEmbedding": (V, E)}
-    for i in range(L):
-        for n in ("firstNorm", "secondNorm"):
-            shapes[f"layer_{i}.{n}.weights"] = (E,)
-            shapes[f"layer_{i}.{n}.biases"] = (E,)
-        for n in ("query", "key", "value", "output"):
-            shapes[f"layer_{i}.attention.{n}.weights"] = (E, E)
-            shapes[f"layer_{i}.attention.{n}.biases"] = (E,)
-        shapes[f"layer_{i}.mlp.layer_0.weights"] = (w["mlp"], E)
-        shapes[f"layer_{i}.mlp.layer_0.biases"] = (w["mlp"],)
-        shapes[f"layer_{i}.mlp.layer_2.weights"] = (E, w["mlp"])
-        shapes[f"layer_{i}.mlp.layer_2.biases"] = (E,)
-    rng = np.random.default_rng(w["seed"])
-    init = {}
-    for name in sorted(shapes):
-        if name.endswith("Norm.weights"):
-            init[name] = np.ones(shapes[name], dtype=np.float32)
-        elif name.endswith("biases"):
-            init[name] = np.zeros(shapes[name], dtype=np.float32)
-        else:
-            init[name] = (rng.standard_normal(shapes[name]) * 0.02).astype(np.float32)
+    init = model.init_parameters(model.parameter_shapes(L, H, D, V, T, w["mlp"]), w["seed"])
     n_steps = args.warmup + args.steps
     brng = np.random.default_rng(w["seed"] + 1000)
     data = []
@@ -717,24 +697,8 @@ def run_config4(args, w):
         ids = brng.integers(0, V, size=(B, T + 1), dtype=np.int64)
         data.append((ids[:, :-1].copy(), ids[:, 1:].copy()))
 
-    def model(params, ids):
-        x = params["tokenEmbedding"][ids] + params["positionEmbedding"][:T].unsqueeze(0)
-        for i in range(L):
-            p = lambda n: params[f"layer_{i}.{n}"]
-            h = torch.nn.functional.layer_norm(x, (E,), p("firstNorm.weights"), p("firstNorm.biases"), 1e-5)
-            split = lambda t: t.view(B, T, H, D).transpose(1, 2).contiguous()
-            q = split(nano.project(h, p("attention.query.weights"), p("attention.query.biases")))
-            k = split(nano.project(h, p("attention.key.weights"), p("attention.key.biases")))
-            v = split(nano.project(h, p("attention.value.weights"), p("attention.value.biases")))
-            o = flash_attention(q, k, v, w["causal"]).transpose(1, 2).reshape(B, T, E)
-            a = nano.project(o, p("attention.output.weights"), p("attention.output.biases"))
-            h2 = torch.nn.functional.layer_norm(a, (E,), p("secondNorm.weights"), p("secondNorm.biases"), 1e-5)
-            m = torch.relu(h2 @ p("mlp.layer_0.weights").T + p("mlp.layer_0.biases"))
-            x = m @ p("mlp.layer_2.weights").T + p("mlp.layer_2.biases")
-        return torch.softmax(x @ params["unEmbedding"].T, -1)
-
     params = {k: torch.tensor(v, device=dev).requires_grad_() for k, v in init.items()}
-    opt = nano.ReferenceAdam(params, lr=w["lr"])
+    opt = model.ReferenceAdam(params, lr=w["lr"])
     losses, times = [], []
     with ClockSampler(local) as clocks:
         for ids_np, tgt_np in data:
@@ -743,18 +707,26 @@ def run_config4(args, w):
             s_ev.record()
             ids = torch.as_tensor(ids_np, device=dev)
             tgt = torch.as_tensor(tgt_np, device=dev)
-            for p_ in params.values():
-                p_.grad = None
-            loss = nano.loss_from_probs(model(params, ids), tgt)
-            loss.backward()
-            opt.step({k: p_.grad for k, p_ in params.items()})
-            lval = float(loss.detach())  # device -> host read of the step's loss
+            loss = model.train_step(params, opt, ids, tgt, L, H, D, w["causal"])
+            lval = float(loss)  # device -> host read of the step's loss
             e_ev.record()
             torch.cuda.synchronize()
             times.append(s_ev.elapsed_time(e_ev))
             losses.append(lval)
     timed = times[args.warmup:]
     ms = float(np.median(timed))
+
+    def time_unit(fn, reps=10):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_ev.record()
+        for _ in range(reps):
+            fn()
+        e_ev.record()
+        torch.cuda.synchronize()
+        return s_ev.elapsed_time(e_ev) / reps
 
     # attention alone: per layer one forward (saving states) and one backward
     q, k, v, do = (torch.randn(B, H, T, D, device=dev) for _ in range(4))
@@ -766,19 +738,29 @@ def run_config4(args, w):
             att.computeBackward(q, k, v, do)
             att.clearCache()
 
-    for _ in range(3):
-        att_unit()
-    torch.cuda.synchronize()
-    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s_ev.record()
-    for _ in range(10):
-        att_unit()
-    e_ev.record()
-    torch.cuda.synchronize()
-    att_ms = s_ev.elapsed_time(e_ev) / 10
+    att_ms = time_unit(att_unit)
+
+    # the two projections alone: per layer forward, input and parameter gradients
+    x, dy = torch.randn(B, T, E, device=dev), torch.randn(B, T, E, device=dev)
+    wts = [torch.randn(E, E, device=dev) * 0.02 for _ in range(4)]
+    bs = [torch.zeros(E, device=dev) for _ in range(4)]
+    gw = [torch.zeros(E, E, device=dev) for _ in range(4)]
+    gb = [torch.zeros(E, device=dev) for _ in range(4)]
+
+    def proj_unit():
+        for _ in range(L):
+            qq, kk, vv = pl.qkv_forward(x, wts[0], bs[0], wts[1], bs[1], wts[2], bs[2], H, D)
+            pl.out_proj_forward(qq, wts[3], bs[3])
+            pl.out_proj_backward(qq, dy, wts[3], gw[3], gb[3])
+            pl.qkv_backward(x, qq, kk, vv, wts[0], wts[1], wts[2], gw[0], gb[0], gw[1], gb[1], gw[2], gb[2])
+
+    proj_ms = time_unit(proj_unit)
+    proj_flops = 24.0 * B * T * E * E * L  # QKV fwd 6, out fwd 2, dx 6 + dW 6, da 2 + dWo 2 (x B*T*E*H*D)
 
     # fp64 restatement of the same training run (loss oracle), on the GPU for
     # the full run; one step of it timed on the host cores as the CPU baseline
+    from oracle import nanogpt_oracle as nano
+
     t0 = time.perf_counter()
     ref_losses = nano.train(init, data, L, H, D, causal=w["causal"], lr=w["lr"], device=str(dev))
     ref_seconds = time.perf_counter() - t0
@@ -798,13 +780,16 @@ def run_config4(args, w):
         "warmup": args.warmup,
         "ms_per_step": round(ms, 3),
         "higher_is_better": True,
-        "dtype": "fp32 I/O; attention on tf32 tcgen05 MMA, the rest PyTorch fp32",
+        "dtype": "fp32 I/O; attention and its QKV / output projections on tf32 tcgen05 MMA, the rest PyTorch fp32",
         "data": "synthetic: weights N(0,0.02) (LayerNorm scale 1, biases 0), token ids uniform [0,65), seeded",
         "config": {"workload": w["desc"], "batch": B, "seq_len": T, "layers": L, "heads": H, "head_dim": D,
                    "causal": w["causal"],
                    "note": "causal (language-model mask)" if w["causal"] else "non-causal, as the reference's attention"},
         "attention_ms_per_step": round(att_ms, 3),
         "attention_share_of_step": round(att_ms / ms, 4),
+        "projection_ms_per_step": round(proj_ms, 3),
+        "projection_share_of_step": round(proj_ms / ms, 4),
+        "projection_tflops": round(proj_flops / (proj_ms * 1e-3) / 1e12, 1),
         "losses": [round(x, 6) for x in losses],
         "restatement_fp64_losses": [round(x, 6) for x in ref_losses],
         "max_abs_loss_diff_vs_restatement": round(max(diffs), 6),

@@ -7,7 +7,7 @@
 // One behaviour differs, on purpose: the reference's forward with state
 // caching stores the attention output in outStates[3] and then releases it
 // (AttentionLayer.cu:88-100), so backward passes an empty tensor to the
-// output projection's backward (AttentionLayer.cu:137), which divides by a
+// output projection's backward (AttentionLayer.cu:136), which divides by a
 // zero sequence length (OutputProjectionLayer.cu:76-77) on every backward
 // through the layer.  Here outStates[3] keeps the attention output until the
 // backward has used it.

@@ -27,39 +27,10 @@
 // Errors: every non-zero status from the library throws std::runtime_error
 // (the reference throws from cudaMakeShared and ignores launch errors).
 #include "ModuleLayer.cu"
-#include "ctfa.h"
+#include "ctfa_dropin.h"
 
 #ifndef FLASH_ATTENTION_LAYER
 #define FLASH_ATTENTION_LAYER
-
-namespace ctfa_dropin {
-
-template <typename T>
-struct DtypeCode;
-template <>
-struct DtypeCode<float> {
-  static constexpr int value = CTFA_DTYPE_F32;
-};
-template <>
-struct DtypeCode<__nv_bfloat16> {
-  static constexpr int value = CTFA_DTYPE_BF16;
-};
-template <>
-struct DtypeCode<__half> {
-  static constexpr int value = CTFA_DTYPE_F16;
-};
-template <>
-struct DtypeCode<double> {
-  static constexpr int value = CTFA_DTYPE_F64;
-};
-
-inline void check(int status, const char* where) {
-  if (status != CTFA_OK)
-    throw std::runtime_error(std::string(where) + ": " + ctfa_status_string(status) + ": " +
-                             ctfa_last_error_message());
-}
-
-}  // namespace ctfa_dropin
 
 template <typename DType = float>
 struct FlashAttentionLayer {

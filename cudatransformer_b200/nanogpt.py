@@ -1,0 +1,114 @@
+"""The reference's NanoGPT training step with the whole
+attention layer on this library: QKV projection, attention and output
+projection run as libctfa_b200.so tcgen05 kernels (autograd.py); embedding,
+LayerNorm, the ReLU MLP, unembedding and softmax are PyTorch ops (plumbing).
+
+Architecture and optimiser follow the reference (cuda_transformer/):
+  * forward, NanoGPT.cu:80-94: token + position embedding -> blocks ->
+    unembedding x U^T (Embedding.cu:360-376) -> softmax;
+  * block, TransformerBlockLayer.cu:60-66: LayerNorm -> attention ->
+    LayerNorm -> Linear, ReLU, Linear, with no residual connections;
+  * LayerNorm eps 1e-5 with biased variance (layer_norm_kernels.cu:34-90);
+    Linear y = x W^T + b, W [out, in] (LinearLayer.cu:13,111);
+  * attention weights read row = output feature (attention_qkv_kernels.cu:92,
+    attention_proj_kernels.cu:83);
+  * loss, loss_kernels.cu:150-189: mean of -log p[target] over all tokens, on
+    the softmax probabilities;
+  * Adam, adam_kernels.cu:44-52 and AdamOptimizer.cu:74-96: the bias-corrected
+    moments are stored back, and the step counter advances twice per step.
+Parameter names are those of the reference's NanoGPT.getParameters().
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from .autograd import flash_attention, out_projection, qkv_projection
+
+
+def parameter_shapes(layers: int, heads: int, head_dim: int, vocab: int, seq_len: int, mlp: int) -> dict:
+    E = heads * head_dim
+    shapes = {"tokenEmbedding": (vocab, E), "positionEmbedding": (seq_len, E), "unEmbedding": (vocab, E)}
+    for i in range(layers):
+        for n in ("firstNorm", "secondNorm"):
+            shapes[f"layer_{i}.{n}.weights"] = (E,)
+            shapes[f"layer_{i}.{n}.biases"] = (E,)
+        for n in ("query", "key", "value", "output"):
+            shapes[f"layer_{i}.attention.{n}.weights"] = (E, E)
+            shapes[f"layer_{i}.attention.{n}.biases"] = (E,)
+        shapes[f"layer_{i}.mlp.layer_0.weights"] = (mlp, E)
+        shapes[f"layer_{i}.mlp.layer_0.biases"] = (mlp,)
+        shapes[f"layer_{i}.mlp.layer_2.weights"] = (E, mlp)
+        shapes[f"layer_{i}.mlp.layer_2.biases"] = (E,)
+    return shapes
+
+
+def init_parameters(shapes: dict, seed: int, std: float = 0.02) -> dict:
+    """N(0, std) weights, LayerNorm scales 1, biases 0 (float32 numpy)."""
+    rng = np.random.default_rng(seed)
+    out = {}
+    for name in sorted(shapes):
+        if name.endswith("Norm.weights"):
+            out[name] = np.ones(shapes[name], dtype=np.float32)
+        elif name.endswith("biases"):
+            out[name] = np.zeros(shapes[name], dtype=np.float32)
+        else:
+            out[name] = (rng.standard_normal(shapes[name]) * std).astype(np.float32)
+    return out
+
+
+def forward(params: dict, ids: torch.Tensor, layers: int, heads: int, head_dim: int, causal: bool) -> torch.Tensor:
+    """Softmax probabilities [B, T, vocab]."""
+    B, T = ids.shape
+    E = heads * head_dim
+    x = params["tokenEmbedding"][ids] + params["positionEmbedding"][:T].unsqueeze(0)
+    for i in range(layers):
+        p = lambda n: params[f"layer_{i}.{n}"]
+        h = torch.nn.functional.layer_norm(x, (E,), p("firstNorm.weights"), p("firstNorm.biases"), 1e-5)
+        q, k, v = qkv_projection(h, p("attention.query.weights"), p("attention.query.biases"),
+                                 p("attention.key.weights"), p("attention.key.biases"),
+                                 p("attention.value.weights"), p("attention.value.biases"), heads, head_dim)
+        a = out_projection(flash_attention(q, k, v, causal), p("attention.output.weights"),
+                           p("attention.output.biases"))
+        h2 = torch.nn.functional.layer_norm(a, (E,), p("secondNorm.weights"), p("secondNorm.biases"), 1e-5)
+        m = torch.relu(h2 @ p("mlp.layer_0.weights").T + p("mlp.layer_0.biases"))
+        x = m @ p("mlp.layer_2.weights").T + p("mlp.layer_2.biases")
+    return torch.softmax(x @ params["unEmbedding"].T, -1)
+
+
+def loss_from_probs(probs: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
+    return -torch.log(probs.gather(-1, target.unsqueeze(-1)).squeeze(-1)).mean()
+
+
+class ReferenceAdam:
+    """Adam as the reference implements it: m and v are stored back already
+    bias-corrected, and the step counter advances twice per step."""
+
+    def __init__(self, params: dict, lr: float = 3e-4, b1: float = 0.9, b2: float = 0.999, eps: float = 1e-8):
+        self.params, self.lr, self.b1, self.b2, self.eps = params, lr, b1, b2, eps
+        self.m = {k: torch.zeros_like(v) for k, v in params.items()}
+        self.v = {k: torch.zeros_like(v) for k, v in params.items()}
+        self.t = 0
+
+    @torch.no_grad()
+    def step(self, grads: dict) -> None:
+        self.t += 1
+        c1, c2 = 1 - self.b1 ** self.t, 1 - self.b2 ** self.t
+        for k, p in self.params.items():
+            g = grads[k]
+            m = self.m[k].mul_(self.b1).add_(g, alpha=1 - self.b1).div_(c1)
+            v = self.v[k].mul_(self.b2).addcmul_(g, g, value=1 - self.b2).div_(c2)
+            p.addcdiv_(m, v.sqrt().add_(self.eps), value=-self.lr)
+        self.t += 1
+
+
+def train_step(params: dict, opt: ReferenceAdam, ids: torch.Tensor, target: torch.Tensor, layers: int, heads: int,
+               head_dim: int, causal: bool) -> torch.Tensor:
+    """One step: forward, loss, backward, Adam update.  Returns the loss
+    (device tensor, before the update)."""
+    for p in params.values():
+        p.grad = None
+    loss = loss_from_probs(forward(params, ids, layers, heads, head_dim, causal), target)
+    loss.backward()
+    opt.step({k: p.grad for k, p in params.items()})
+    return loss.detach()

@@ -1,18 +1,29 @@
 // dropin_check.cu -- TEST INFRASTRUCTURE ONLY.  Compiles the reference's own
 // AttentionLayer / TransformerBlockLayer (cuda_transformer/*.cu, unmodified,
 // from the reference tree) against cudatransformer_b200/FlashAttentionLayer.cu,
+// QKVProjectionLayer.cu and OutputProjectionLayer.cu (the drop-ins),
 // for every element type the reference instantiates (float, double, half,
 // bfloat16; cuda_transformer.cu:839-842), and exposes one C entry point that
 // runs the reference's AttentionLayer<float>::forward through it.  It proves
 // the drop-in compiles where the reference's layer did, and lets a GPU test
 // compare the composed layer with an fp64 restatement.
 #include "FlashAttentionLayer.cu"  // ours: same include guard as the reference file
-#include "TransformerBlockLayer.cu"  // reference: pulls AttentionLayer.cu -> our layer
+#include "OutputProjectionLayer.cu"  // ours, likewise
+#include "QKVProjectionLayer.cu"  // ours, likewise
+#include "TransformerBlockLayer.cu"  // reference: pulls AttentionLayer.cu -> our layers
 
 template struct FlashAttentionLayer<float>;
 template struct FlashAttentionLayer<double>;
 template struct FlashAttentionLayer<__half>;
 template struct FlashAttentionLayer<__nv_bfloat16>;
+template struct QKVProjectionLayer<float>;
+template struct QKVProjectionLayer<double>;
+template struct QKVProjectionLayer<__half>;
+template struct QKVProjectionLayer<__nv_bfloat16>;
+template struct OutputProjectionLayer<float>;
+template struct OutputProjectionLayer<double>;
+template struct OutputProjectionLayer<__half>;
+template struct OutputProjectionLayer<__nv_bfloat16>;
 template struct AttentionLayer<float>;
 template struct AttentionLayer<__nv_bfloat16>;
 template struct TransformerBlockLayer<float>;

@@ -59,3 +59,30 @@ def test_nanogpt_restatement_trains_the_same_with_our_attention(cuda_device):
     lib = lambda q, k, v, causal: flash_attention(q.float(), k.float(), v.float(), causal).double()
     ours = nano.train(init, data, L, H, D, device=str(cuda_device), attention=lib)
     assert max(abs(a - b) for a, b in zip(ours, ref)) < 1e-4
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_package_nanogpt_step_tracks_the_fp64_restatement(cuda_device, causal):
+    """cudatransformer_b200.nanogpt (fp32; QKV projection, attention and
+    output projection on the library's tf32 kernels, the rest PyTorch fp32)
+    against the fp64 restatement: same weights, tokens and reference Adam,
+    four steps; every loss within 2e-3."""
+    from cudatransformer_b200 import nanogpt as model
+    from oracle import nanogpt_oracle as nano
+
+    L, H, D, V, T, B = 2, 2, 64, 65, 128, 4
+    init = model.init_parameters(model.parameter_shapes(L, H, D, V, T, 4 * H * D), seed=8)
+    rng = np.random.default_rng(9)
+    data = []
+    for _ in range(4):
+        ids = rng.integers(0, V, size=(B, T + 1))
+        data.append((ids[:, :-1], ids[:, 1:]))
+    ref = nano.train(init, data, L, H, D, causal=causal, device=str(cuda_device))
+    params = {k: torch.tensor(v, device=cuda_device).requires_grad_() for k, v in init.items()}
+    opt = model.ReferenceAdam(params)
+    ours = []
+    for ids, tgt in data:
+        ids_t = torch.as_tensor(ids, device=cuda_device)
+        tgt_t = torch.as_tensor(tgt, device=cuda_device)
+        ours.append(float(model.train_step(params, opt, ids_t, tgt_t, L, H, D, causal)))
+    assert max(abs(a - b) for a, b in zip(ours, ref)) < 2e-3, (ours, ref)
