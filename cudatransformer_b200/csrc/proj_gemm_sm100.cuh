@@ -384,7 +384,7 @@ __global__ void __launch_bounds__(192, 2)
         }
       }
       tma_store_commit();
-      tma_store_wait_all();
+      tma_store_wait_read();  // smem must stay valid until read; the writes complete with the grid
     }
     }
   }

@@ -170,7 +170,15 @@ def test_autograd_projection_gradients(cuda_device, dt):
     ro = torch.softmax(s, -1) @ rv
     ry = ro.transpose(1, 2).reshape(B, T, H * D) @ rwo.T + rbo
     ry.backward(dy.double())
-    tol = 2e-3 if dt == torch.float32 else 2e-2
+    # three tf32 (bf16) stages in a row -> 5e-3 (2e-2); per-kernel bounds are
+    # checked above.  The exact gradient of the key bias is zero (a constant
+    # added to every key shifts each score row by q.b, which the softmax
+    # ignores), so bk is checked against the scale of the query-bias gradient.
+    tol = 5e-3 if dt == torch.float32 else 2e-2
     _check(y, ry.detach().cpu().numpy(), tol, "y")
     for got, want, n in zip(leaves, ref, ("x", "wq", "bq", "wk", "bk", "wv", "bv", "wo", "bo")):
+        if n == "bk":
+            scale = rbq.grad.abs().max().item()
+            assert got.grad.double().abs().max().item() < tol * scale, "grad bk not ~0"
+            continue
         _check(got.grad, want.grad.cpu().numpy(), tol, f"grad {n}")
