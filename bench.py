@@ -57,6 +57,10 @@ WORKLOADS = {
     "config4": dict(desc="BASELINE config 4: NanoGPT training step (6 layers, d=384, 6 heads x 64, T=256, vocab 65, "
                          "batch 64, fp32, Adam lr 3e-4)", B=64, H=6, T=256, D=64, dtype="f32", causal=False,
                     layers=6, vocab=65, mlp=1536, lr=3e-4, seed=3),
+    "proj_config4": dict(desc="QKV + output projection GEMMs of one config-4 block (B=64, T=256, E=384, 6 heads x 64), "
+                              "fp32", B=64, T=256, E=384, H=6, D=64, dtype="f32", seed=5),
+    "proj_bf16": dict(desc="QKV + output projection GEMMs, bf16, B=8, T=2048, E=2048, 16 heads x 128", B=8, T=2048,
+                      E=2048, H=16, D=128, dtype="bf16", seed=6),
     "config4causal": dict(desc="BASELINE config 4 with the causal mask (language-model semantics)", B=64, H=6, T=256,
                           D=64, dtype="f32", causal=True, layers=6, vocab=65, mlp=1536, lr=3e-4, seed=3),
 }
@@ -805,6 +809,167 @@ def run_config4(args, w):
     print(json.dumps(out), flush=True)
 
 
+def run_projections(args, w):
+    """The six projection GEMMs of one attention layer (QKV forward, output
+    forward, output backward: dWo + dbo and da, QKV backward: dW + db and dx)
+    through the C ABI.  The step and each GEMM alone are captured once into
+    CUDA graphs, so the timed replays measure the device (at the config-4
+    shapes a GEMM is shorter than the host's cost of preparing its launch);
+    CUDA events on the replay stream.  value = the algorithmic FLOPs
+    (24 * B*T*E*H*D) per step time."""
+    import numpy as np
+    import torch
+
+    from cudatransformer_b200 import projection_layers as pl
+
+    rank, world, local = dist_init(args.gpus)
+    if rank != 0:
+        return
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    B, T, E, H, D = w["B"], w["T"], w["E"], w["H"], w["D"]
+    HD = H * D
+    dt = torch.float32 if w["dtype"] == "f32" else torch.bfloat16
+    g = torch.Generator(device="cpu").manual_seed(w["seed"])
+    mk = lambda *shape, scale=1.0: (torch.randn(*shape, generator=g) * scale).to(dt).to(dev)
+    x, dy = mk(B, T, E), mk(B, T, E)
+    wq, wk, wv = (mk(HD, E, scale=E ** -0.5) for _ in range(3))
+    bq, bk, bv = (mk(HD, scale=0.1) for _ in range(3))
+    wo, bo = mk(E, HD, scale=HD ** -0.5), mk(E, scale=0.1)
+    gw = [torch.zeros_like(t) for t in (wq, wk, wv, wo)]
+    gb = [torch.zeros_like(t) for t in (bq, bk, bv, bo)]
+    q, k, v = (torch.empty(B, H, T, D, dtype=dt, device=dev) for _ in range(3))
+    lib = pl._lib.load()
+    code = pl._code(x)
+    P = lambda t: None if t is None else t.data_ptr()
+    y, dx, da = torch.empty(B, T, E, dtype=dt, device=dev), torch.empty(B, T, E, dtype=dt, device=dev), \
+        torch.empty(B, H, T, D, dtype=dt, device=dev)
+
+    def stream_ptr():
+        return torch.cuda.current_stream(dev).cuda_stream
+
+    # the C ABI directly (preallocated outputs), so each captured graph holds
+    # exactly one library launch
+    gemms = {
+        "qkv_fwd": lambda: lib.ctfa_qkv_forward(P(x), P(wq), P(bq), P(wk), P(bk), P(wv), P(bv), P(q), P(k), P(v),
+                                                B, T, E, H, D, code, stream_ptr()),
+        "out_fwd": lambda: lib.ctfa_out_proj_forward(P(q), P(wo), P(bo), P(y), B, T, E, H, D, code, stream_ptr()),
+        "out_dw": lambda: lib.ctfa_out_proj_backward(P(q), P(dy), None, P(gw[3]), P(gb[3]), None, B, T, E, H, D,
+                                                     code, stream_ptr()),
+        "out_da": lambda: lib.ctfa_out_proj_backward(None, P(dy), P(wo), None, None, P(da), B, T, E, H, D, code,
+                                                     stream_ptr()),
+        "qkv_dw": lambda: lib.ctfa_qkv_backward(P(x), P(q), P(k), P(v), None, None, None, P(gw[0]), P(gb[0]),
+                                                P(gw[1]), P(gb[1]), P(gw[2]), P(gb[2]), None, B, T, E, H, D, code,
+                                                stream_ptr()),
+        "qkv_dx": lambda: lib.ctfa_qkv_backward(None, P(q), P(k), P(v), P(wq), P(wk), P(wv), None, None, None, None,
+                                                None, None, P(dx), B, T, E, H, D, code, stream_ptr()),
+    }
+    names = list(gemms)
+    f1 = 2.0 * B * T * E * HD
+    flops = {"qkv_fwd": 3 * f1, "out_fwd": f1, "out_dw": f1, "out_da": f1, "qkv_dw": 3 * f1, "qkv_dx": 3 * f1}
+
+    def run(fn):
+        st = fn()
+        if st != 0:
+            raise RuntimeError(f"projection call failed: {pl._lib.status_name(st)}: {pl._lib.last_error()}")
+
+    def step():
+        for n in names:
+            run(gemms[n])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream(dev)
+    graphs = {}
+    with torch.cuda.stream(side):
+        for n in names + ["step"]:
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=side):
+                step() if n == "step" else run(gemms[n])
+            graphs[n] = gr
+    torch.cuda.synchronize()
+
+    def timed(gr, reps):
+        gr.replay()
+        torch.cuda.synchronize()
+        s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_ev.record()
+        for _ in range(reps):
+            gr.replay()
+        e_ev.record()
+        torch.cuda.synchronize()
+        return s_ev.elapsed_time(e_ev) / reps
+
+    with ClockSampler(local) as clocks:
+        ms = timed(graphs["step"], args.steps)
+        per = {n: timed(graphs[n], args.steps) for n in names}
+    total = sum(flops.values())
+    value = total / (ms * 1e-3) / 1e12
+    dom = max(per, key=per.get)
+    if dt == torch.float32:
+        peak, peak_note = tf32_peak_tflops(), "tf32 dense, cuBLAS 8192^3 measured in this run (best of 10)"
+    else:
+        peak = float(measured_peaks().get("bf16_tflops", 1590.0))
+        peak_note = "bf16 dense burst, MEASURED_PEAKS.json"
+    achieved = flops[dom] / (per[dom] * 1e-3) / 1e12
+
+    # CPU baseline: the same six products with PyTorch fp32 on the host cores,
+    # on a sample of the rows (the reference has no CPU implementation)
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    Bs = max(1, min(B, 2))
+    xr = x[:Bs].float().cpu().reshape(-1, E)
+    dyr = dy[:Bs].float().cpu().reshape(-1, E)
+    wcat = torch.cat([wq, wk, wv], 0).float().cpu()
+    woc = wo.float().cpu()
+
+    def cpu_step():
+        qkv = xr @ wcat.T
+        a = qkv[:, :HD]
+        a @ woc.T
+        dyr.T @ a
+        dyr @ woc
+        qkv.T @ xr
+        qkv @ wcat
+
+    cpu_step()
+    t0, n_cpu = time.perf_counter(), 0
+    while time.perf_counter() - t0 < 3.0:
+        cpu_step()
+        n_cpu += 1
+    cpu_s = (time.perf_counter() - t0) / n_cpu
+    cpu_value = total * Bs / B / cpu_s / 1e12
+    del graphs
+    out = {
+        "metric": "projection GEMMs of one attention layer, TFLOP/s",
+        "value": round(value, 1),
+        "unit": "TFLOP/s",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp32 I/O, tf32 tcgen05 MMA" if dt == torch.float32 else "bf16 I/O, bf16 tcgen05 MMA",
+        "data": "synthetic: N(0,1) activations and gradients, weights N(0,1/fan_in), seeded",
+        "config": {"workload": w["desc"], "batch": B, "seq_len": T, "E": E, "heads": H, "head_dim": D,
+                   "l2": "inputs reused across replays (the L2-resident regime of a training step)",
+                   "timing": "CUDA-graph replays (one graph per GEMM, one for the step)"},
+        "kernels": {n: {"ms": round(per[n], 4), "tflops": round(flops[n] / (per[n] * 1e-3) / 1e12, 1)}
+                    for n in names},
+        "roofline": {"kernel": dom, "bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1),
+                     "unit": "TFLOP/s", "frac": round(achieved / peak, 3), "peak_source": peak_note,
+                     "traffic": None},
+        "cpu_baseline": {"value": round(cpu_value, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                         "sample": f"the same six GEMMs on {Bs} of {B} sequences, PyTorch fp32 on the host"},
+        "gpu_launches": 6 * args.steps,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(out), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -818,6 +983,8 @@ def main():
     w = WORKLOADS[args.workload]
     if args.workload in ("config4", "config4causal"):
         run_config4(args, w)
+    elif args.workload.startswith("proj_"):
+        run_projections(args, w)
     elif args.impl == "reference":
         run_reference(args, w)
     else:

@@ -71,7 +71,7 @@ template <typename DType = float> struct AttentionLayer : public Layer<DType> {
 
     Tensor<DType> slotTensor(const Slot& s, bool grad) {
         std::shared_ptr<DType[]>& buf = grad ? *s.grad : *s.param;
-        if (grad && buf == nullptr) buf = cudaMakeShared<DType>(s.count());  // lazily allocated, zero-filled
+        if (grad && buf == nullptr) buf = ctfa_dropin::stream_buffer<DType>(s.count(), true);  // lazily, zero-filled
         return Tensor<DType>(buf, s.shape);
     }
 
@@ -79,8 +79,8 @@ template <typename DType = float> struct AttentionLayer : public Layer<DType> {
         auto copy = std::make_shared<AttentionLayer<DType>>(inputDim, numHeads, headDim);
         std::array<Slot, 8> mine = slots(), theirs = copy->slots();
         for (size_t i = 0; i < mine.size(); ++i)
-            cudaMemcpy(theirs[i].param->get(), mine[i].param->get(), mine[i].count() * sizeof(DType),
-                       cudaMemcpyDeviceToDevice);
+            cudaMemcpyAsync(theirs[i].param->get(), mine[i].param->get(), mine[i].count() * sizeof(DType),
+                            cudaMemcpyDeviceToDevice, 0);
         return copy;
     }
 
@@ -143,7 +143,7 @@ template <typename DType = float> struct AttentionLayer : public Layer<DType> {
 
     void sgdUpdate(DType lr) override {
         for (const Slot& s : slots()) {
-            if (*s.grad == nullptr) *s.grad = cudaMakeShared<DType>(s.count());
+            if (*s.grad == nullptr) *s.grad = ctfa_dropin::stream_buffer<DType>(s.count(), true);
             runSgdUpdate<DType>(*s.param, *s.grad, lr, (int)s.count());
         }
     }

@@ -14,8 +14,11 @@
 // Build: put this directory before the reference's cuda_transformer/ on the
 // include path and include this header before the reference's headers (or
 // replace the reference file with it), add include/ to the path and link
-// libctfa_b200.so.  Allocation follows the reference: outputs and caches are
-// Tensor / cudaMakeShared buffers on the legacy default stream.
+// libctfa_b200.so.  Outputs and caches are Tensor<DType> / shared_ptr buffers
+// on the default stream like the reference's, but stream-ordered
+// (cudaMallocAsync / cudaFreeAsync, ctfa_dropin.h): no device-wide
+// synchronisation per allocation (the reference's cudaMakeShared has one,
+// headers.cu:206-207).
 //
 // Additions (all defaulted, existing call sites unchanged):
 //   * bool causal (constructor's optional third argument, default false = the
@@ -63,15 +66,17 @@ struct FlashAttentionLayer {
     const int batchSize = queries.shape()[0];
     const int sequenceLength = queries.shape()[2];
     const size_t rows = (size_t)batchSize * numHeads * sequenceLength;
-    Tensor<DType> output(queries.shape().toVector());
-    std::shared_ptr<float[]> lse = cudaMakeShared<float>(rows);
+    Tensor<DType> output = ctfa_dropin::stream_tensor<DType>(queries.shape().toVector());
+    std::shared_ptr<float[]> lse = ctfa_dropin::stream_buffer<float>(rows);
     runForward(queries, keys, values, output.data(), lse.get(), batchSize, sequenceLength);
     if (saveStates) {
       cachedLSE = lse;
-      cachedMaxScores = cudaMakeShared<DType>(rows);
+      cachedMaxScores = ctfa_dropin::stream_buffer<DType>(rows);
       castKernel<float, DType><<<(rows + 255) / 256, 256>>>(lse.get(), cachedMaxScores.get(), rows);
-      cachedDenominators = cudaMakeShared<DType>(rows, (DType)1.0f);
-      cachedOutput = cudaCloneShared<DType>(output.dataPtr(), output.size());
+      cachedDenominators = ctfa_dropin::stream_buffer<DType>(rows);
+      fillKernel<DType><<<(rows + 255) / 256, 256>>>(cachedDenominators.get(), rows, (DType)1.0f);
+      cachedOutput = ctfa_dropin::stream_buffer<DType>(output.size());
+      cudaMemcpyAsync(cachedOutput.get(), output.data(), output.size() * sizeof(DType), cudaMemcpyDeviceToDevice, 0);
       cachedBatchSize = batchSize;
       cachedSequenceLength = sequenceLength;
     }
@@ -85,9 +90,9 @@ struct FlashAttentionLayer {
   std::array<Tensor<DType>, 3> computeBackward(const Tensor<DType>& queries, const Tensor<DType>& keys,
                                                const Tensor<DType>& values, const Tensor<DType>& outputGrad) {
     std::array<Tensor<DType>, 3> grads;
-    grads[0] = Tensor<DType>(queries.shape());
-    grads[1] = Tensor<DType>(keys.shape());
-    grads[2] = Tensor<DType>(values.shape());
+    grads[0] = ctfa_dropin::stream_tensor<DType>(queries.shape().toVector());
+    grads[1] = ctfa_dropin::stream_tensor<DType>(keys.shape().toVector());
+    grads[2] = ctfa_dropin::stream_tensor<DType>(values.shape().toVector());
     const int batchSize = queries.shape()[0];
     const int sequenceLength = queries.shape()[2];
     const size_t rows = (size_t)batchSize * numHeads * sequenceLength;
@@ -96,13 +101,13 @@ struct FlashAttentionLayer {
     std::shared_ptr<float[]> lse = cachedLSE;
     if (output == nullptr || lse == nullptr || cachedBatchSize != batchSize ||
         cachedSequenceLength != sequenceLength) {
-      output = cudaMakeShared<DType>(rows * headDim);
-      lse = cudaMakeShared<float>(rows);
+      output = ctfa_dropin::stream_buffer<DType>(rows * headDim);
+      lse = ctfa_dropin::stream_buffer<float>(rows);
       runForward(queries, keys, values, output.get(), lse.get(), batchSize, sequenceLength);
     }
     const int code = ctfa_dropin::DtypeCode<DType>::value;
     const size_t wsBytes = ctfa_backward_workspace_bytes(batchSize, numHeads, sequenceLength, headDim, code);
-    std::shared_ptr<unsigned char[]> ws = cudaMakeShared<unsigned char>(wsBytes > 0 ? wsBytes : 256);
+    std::shared_ptr<unsigned char[]> ws = ctfa_dropin::stream_buffer<unsigned char>(wsBytes > 0 ? wsBytes : 256);
     ctfa_dropin::check(ctfa_backward(queries.get(), keys.get(), values.get(), output.get(), outputGrad.get(),
                                      lse.get(), grads[0].data(), grads[1].data(), grads[2].data(), ws.get(),
                                      wsBytes, batchSize, numHeads, sequenceLength, headDim, code, causal ? 1 : 0,
@@ -124,7 +129,7 @@ struct FlashAttentionLayer {
                   DType* output, float* lse, int batchSize, int sequenceLength) {
     const int code = ctfa_dropin::DtypeCode<DType>::value;
     const size_t wsBytes = ctfa_forward_workspace_bytes(batchSize, numHeads, sequenceLength, headDim, code);
-    std::shared_ptr<unsigned char[]> ws = wsBytes > 0 ? cudaMakeShared<unsigned char>(wsBytes) : nullptr;
+    std::shared_ptr<unsigned char[]> ws = ctfa_dropin::stream_buffer<unsigned char>(wsBytes);
     ctfa_dropin::check(ctfa_forward(queries.get(), keys.get(), values.get(), output, lse, batchSize, numHeads,
                                     sequenceLength, headDim, code, causal ? 1 : 0, ws.get(), wsBytes, nullptr),
                        "ctfa_forward");

@@ -11,7 +11,8 @@
 // Semantics kept: weightsProj [inputDim rows of headDim*numHeads] read row =
 // output feature (attention_proj_kernels.cu:83), zero-filled at construction;
 // gradients allocated zero-filled by the first backward and ACCUMULATED by
-// every backward; outputs freshly allocated.
+// every backward; outputs freshly allocated.  Every buffer is stream-ordered
+// on the default stream (ctfa_dropin.h): nothing synchronises the device.
 #include "ModuleLayer.cu"
 #include "ctfa_dropin.h"
 
@@ -31,15 +32,15 @@ struct OutputProjectionLayer {
 
   OutputProjectionLayer(int inputDim, int headDim, int numHeads)
       : inputDim(inputDim), headDim(headDim), numHeads(numHeads) {
-    weightsProj = cudaMakeShared<DType>((size_t)headDim * numHeads * inputDim);
-    biasesProj = cudaMakeShared<DType>(inputDim);
+    weightsProj = ctfa_dropin::stream_buffer<DType>((size_t)headDim * numHeads * inputDim, true);
+    biasesProj = ctfa_dropin::stream_buffer<DType>(inputDim, true);
   }
 
   std::shared_ptr<OutputProjectionLayer<DType>> clone() const {
     auto c = std::make_shared<OutputProjectionLayer<DType>>(inputDim, headDim, numHeads);
-    cudaMemcpy(c->weightsProj.get(), weightsProj.get(), (size_t)headDim * numHeads * inputDim * sizeof(DType),
-               cudaMemcpyDeviceToDevice);
-    cudaMemcpy(c->biasesProj.get(), biasesProj.get(), inputDim * sizeof(DType), cudaMemcpyDeviceToDevice);
+    cudaMemcpyAsync(c->weightsProj.get(), weightsProj.get(), (size_t)headDim * numHeads * inputDim * sizeof(DType),
+                    cudaMemcpyDeviceToDevice, 0);
+    cudaMemcpyAsync(c->biasesProj.get(), biasesProj.get(), inputDim * sizeof(DType), cudaMemcpyDeviceToDevice, 0);
     return c;
   }
 
@@ -47,7 +48,7 @@ struct OutputProjectionLayer {
   Tensor<DType> forward(Tensor<DType> input) {
     const int seq = rows(input);
     const int batch = input.size() / (seq * (headDim * numHeads));
-    Tensor<DType> output(std::vector<size_t>{(size_t)batch, (size_t)seq, (size_t)inputDim});
+    Tensor<DType> output = ctfa_dropin::stream_tensor<DType>({(size_t)batch, (size_t)seq, (size_t)inputDim});
     ctfa_dropin::check(ctfa_out_proj_forward(input.get(), weightsProj.get(), biasesProj.get(), output.data(), batch,
                                              seq, inputDim, numHeads, headDim, ctfa_dropin::DtypeCode<DType>::value,
                                              nullptr),
@@ -58,12 +59,12 @@ struct OutputProjectionLayer {
   /** Accumulates the parameter gradients; returns the gradient of the attention output. */
   Tensor<DType> backward(Tensor<DType> input, Tensor<DType> gradOutput) {
     if (weightsProjGrad == nullptr) {
-      weightsProjGrad = cudaMakeShared<DType>((size_t)headDim * numHeads * inputDim);
-      biasesProjGrad = cudaMakeShared<DType>(inputDim);
+      weightsProjGrad = ctfa_dropin::stream_buffer<DType>((size_t)headDim * numHeads * inputDim, true);
+      biasesProjGrad = ctfa_dropin::stream_buffer<DType>(inputDim, true);
     }
     const int seq = rows(input);
     const int batch = input.size() / (seq * (headDim * numHeads));
-    Tensor<DType> inputGrad(input.shape());
+    Tensor<DType> inputGrad = ctfa_dropin::stream_tensor<DType>(input.shape().toVector());
     ctfa_dropin::check(ctfa_out_proj_backward(input.get(), gradOutput.get(), weightsProj.get(), weightsProjGrad.get(),
                                               biasesProjGrad.get(), inputGrad.data(), batch, seq, inputDim,
                                               numHeads, headDim, ctfa_dropin::DtypeCode<DType>::value, nullptr),

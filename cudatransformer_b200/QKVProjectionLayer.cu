@@ -13,6 +13,8 @@
 // feature (attention_qkv_kernels.cu:92), zero-filled at construction;
 // gradients allocated zero-filled by the first backward and ACCUMULATED by
 // every backward (the reference's atomicAdd); inputGrad freshly allocated.
+// Every buffer is stream-ordered on the default stream (ctfa_dropin.h), so
+// neither construction nor a call synchronises the device.
 // Errors: a failing library call throws std::runtime_error.
 #include <array>
 
@@ -43,8 +45,8 @@ struct QKVProjectionLayer {
 
   QKVProjectionLayer(int inputDim, int numHeads, int headDim)
       : inputDim(inputDim), numHeads(numHeads), headDim(headDim) {
-    for (std::shared_ptr<DType[]>* w : weights()) *w = cudaMakeShared<DType>(projSize());
-    for (std::shared_ptr<DType[]>* b : biases()) *b = cudaMakeShared<DType>(biasSize());
+    for (std::shared_ptr<DType[]>* w : weights()) *w = ctfa_dropin::stream_buffer<DType>(projSize(), true);
+    for (std::shared_ptr<DType[]>* b : biases()) *b = ctfa_dropin::stream_buffer<DType>(biasSize(), true);
   }
 
   std::shared_ptr<QKVProjectionLayer<DType>> clone() const {
@@ -54,8 +56,8 @@ struct QKVProjectionLayer {
     const std::array<std::shared_ptr<DType[]>*, 6> dst = {&c->weightsQuery, &c->weightsKey, &c->weightsValue,
                                                           &c->biasesQuery,  &c->biasesKey,  &c->biasesValue};
     for (int i = 0; i < 6; ++i)
-      cudaMemcpy(dst[i]->get(), src[i]->get(), (i < 3 ? projSize() : biasSize()) * sizeof(DType),
-                 cudaMemcpyDeviceToDevice);
+      cudaMemcpyAsync(dst[i]->get(), src[i]->get(), (i < 3 ? projSize() : biasSize()) * sizeof(DType),
+                      cudaMemcpyDeviceToDevice, 0);
     return c;
   }
 
@@ -64,7 +66,8 @@ struct QKVProjectionLayer {
     const int seq = rows(input);
     const int batch = input.size() / (seq * inputDim);
     const std::vector<size_t> shape = {(size_t)batch, (size_t)numHeads, (size_t)seq, (size_t)headDim};
-    Tensor<DType> q(shape), k(shape), v(shape);
+    Tensor<DType> q = ctfa_dropin::stream_tensor<DType>(shape), k = ctfa_dropin::stream_tensor<DType>(shape),
+                  v = ctfa_dropin::stream_tensor<DType>(shape);
     ctfa_dropin::check(ctfa_qkv_forward(input.get(), weightsQuery.get(), biasesQuery.get(), weightsKey.get(),
                                         biasesKey.get(), weightsValue.get(), biasesValue.get(), q.data(), k.data(),
                                         v.data(), batch, seq, inputDim, numHeads, headDim,
@@ -79,10 +82,10 @@ struct QKVProjectionLayer {
     const int seq = rows(input);
     const int batch = input.size() / (seq * inputDim);
     if (weightsQueryGrad == nullptr) {
-      for (std::shared_ptr<DType[]>* g : weightGrads()) *g = cudaMakeShared<DType>(projSize());
-      for (std::shared_ptr<DType[]>* g : biasGrads()) *g = cudaMakeShared<DType>(biasSize());
+      for (std::shared_ptr<DType[]>* g : weightGrads()) *g = ctfa_dropin::stream_buffer<DType>(projSize(), true);
+      for (std::shared_ptr<DType[]>* g : biasGrads()) *g = ctfa_dropin::stream_buffer<DType>(biasSize(), true);
     }
-    Tensor<DType> inputGrad(input.shape().toVector());
+    Tensor<DType> inputGrad = ctfa_dropin::stream_tensor<DType>(input.shape().toVector());
     ctfa_dropin::check(
         ctfa_qkv_backward(input.get(), queryGrad.get(), keyGrad.get(), valueGrad.get(), weightsQuery.get(),
                           weightsKey.get(), weightsValue.get(), weightsQueryGrad.get(), biasesQueryGrad.get(),

@@ -19,7 +19,15 @@ namespace {
 
 using namespace ctfa;
 
-constexpr int kProjStages = 3;
+// Pipeline depth per kind.  Row-wise kinds: 2 stages (64 KB, also the fp32
+// staging tile) so that three CTAs share an SM (3 x 128 TMEM columns): the
+// output-projection and dx/da grids (B*T/128 x E/128 CTAs, 384 at config 4)
+// then run in one wave.  Weight-gradient kinds: 3 stages, two CTAs per SM
+// (their accumulator is 256 TMEM columns wide for the bias-gradient block).
+template <int KIND>
+constexpr int proj_stages() {
+  return (KIND == kProjQkvDw || KIND == kProjOutDw) ? 3 : 2;
+}
 
 // ---------------------------------------------------------------------------
 // SIMT kernels: one thread per output element, accumulation in double for
@@ -223,8 +231,9 @@ int map_weight(CUtensorMap* m, const void* p, const ProjShape& s, int rows, int 
 template <typename DT, int KIND>
 int launch_proj_tc(ProjParams p, const CUtensorMap (&ta)[3], const CUtensorMap (&tb)[3], const CUtensorMap (&to)[3],
                    cudaStream_t stream) {
-  using C = ProjConfig<DT, KIND, kProjStages>;
-  auto kern = proj_gemm_sm100<DT, KIND, kProjStages>;
+  constexpr int kStages = proj_stages<KIND>();
+  using C = ProjConfig<DT, KIND, kStages>;
+  auto kern = proj_gemm_sm100<DT, KIND, kStages>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(proj_gemm_sm100)");
   p.wait_limit_ns = g_wait_limit_ns;
@@ -262,10 +271,11 @@ ProjParams proj_params(const ProjShape& s) {
 
 int ceil_div(long long a, long long b) { return (int)((a + b - 1) / b); }
 
-// Split count for the weight-gradient GEMMs: about two CTAs per SM in total,
-// at least two k-steps per CTA.
+// Split count for the weight-gradient GEMMs: as many CTAs as fit in ONE wave
+// (two per SM, see proj_stages), at least two k-steps per CTA.  Rounding up instead would put
+// a few CTAs into a second wave and double the kernel's duration.
 int dw_splits(int tiles, int ksteps) {
-  const long long want = (2 * sm_count() + tiles - 1) / tiles;
+  const long long want = (2 * sm_count()) / tiles;
   return (int)std::max<long long>(1, std::min<long long>(want, ksteps / 2));
 }
 

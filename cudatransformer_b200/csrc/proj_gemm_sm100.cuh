@@ -98,7 +98,7 @@ __device__ __forceinline__ DT proj_from_float(float x) {
 }
 
 template <typename DT, int KIND, int STAGES>
-__global__ void __launch_bounds__(192, 2)
+__global__ void __launch_bounds__(192, STAGES == 2 ? 3 : 2)
     proj_gemm_sm100(const __grid_constant__ CUtensorMap ta0, const __grid_constant__ CUtensorMap ta1,
                     const __grid_constant__ CUtensorMap ta2, const __grid_constant__ CUtensorMap tb0,
                     const __grid_constant__ CUtensorMap tb1, const __grid_constant__ CUtensorMap tb2,

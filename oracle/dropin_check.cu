@@ -52,3 +52,29 @@ extern "C" int dropin_attention_forward(const float* x, const float* wq, const f
     return -1;
   }
 }
+
+// Device-resident variant (x, w*, y device pointers; biases zero): builds the
+// reference's AttentionLayer<float> over the drop-ins, runs forward, copies y
+// with a stream-ordered copy and returns WITHOUT synchronising, so that a test
+// can check that nothing in construction, forward or teardown waited for the
+// device (the drop-ins' buffers are stream-ordered).
+extern "C" int dropin_attention_forward_device(const float* x, const float* wq, const float* wk, const float* wv,
+                                               const float* wo, float* y, int B, int N, int E, int H, int causal) {
+  try {
+    const int D = E / H;
+    AttentionLayer<float> layer(E, H, D);
+    layer.flashAttn.causal = causal != 0;
+    auto view = [](const float* p, std::vector<size_t> shape) {
+      return Tensor<float>(std::shared_ptr<float[]>(const_cast<float*>(p), [](float*) {}), shape);
+    };
+    layer.setQueryWeights(view(wq, {(size_t)E, (size_t)E}));
+    layer.setKeyWeights(view(wk, {(size_t)E, (size_t)E}));
+    layer.setValueWeights(view(wv, {(size_t)E, (size_t)E}));
+    layer.setOutputWeights(view(wo, {(size_t)E, (size_t)E}));
+    Tensor<float> out = layer.forward(view(x, {(size_t)B, (size_t)N, (size_t)E}));
+    cudaMemcpyAsync(y, out.data(), out.size() * sizeof(float), cudaMemcpyDeviceToDevice, 0);
+    return (int)cudaGetLastError();
+  } catch (const std::exception&) {
+    return -1;
+  }
+}

@@ -96,6 +96,21 @@ def out_proj_backward(a, dy, wo):
     return da, dyr.T @ _rows(a), dyr.sum(0)
 
 
+def reference_bias_grad(g_rows) -> np.ndarray:
+    """What the reference's bias-gradient code actually accumulates: only rows
+    r = 0, 32, 64, ... of the [B*T, N] gradient.  In qkvBackwardWB
+    (attention_qkv_kernels.cu:233-237) the bias sum runs only in the thread
+    with inputIdx == 0 and reads its own tile column threadIdx.x = 0, i.e. row
+    tile + 0 of each 32-row tile; projBackwardWB
+    (attention_proj_kernels.cu:188, :195-197) sums per thread column but adds
+    only the inputDimIdx == 0 thread's partial (rows tile + 0) to the
+    gradient.  BLOCKDIM = 32 (ModuleLayer.cu:6).  The true bias gradient sums
+    every row; tests use this emulation to confirm the reference's behaviour
+    on the GPU, not as a target."""
+    g = np.asarray(g_rows, np.float64)
+    return g[::32].sum(0)
+
+
 def max_rel_err(x, ref) -> float:
     """max |x - ref| / max |ref| (norm-wise relative error)."""
     x = np.asarray(x, np.float64)
