@@ -913,6 +913,12 @@ def run_projections(args, w):
         peak = float(measured_peaks().get("bf16_tflops", 1590.0))
         peak_note = "bf16 dense burst, MEASURED_PEAKS.json"
     achieved = flops[dom] / (per[dom] * 1e-3) / 1e12
+    traffic = None
+    try:
+        entry = json.loads((ROOT / "profiles" / "roofline_traffic.json").read_text()).get(f"{args.workload}/{dom}")
+        traffic = entry["dram_bytes_per_launch"] if entry else None
+    except (OSError, ValueError, KeyError):
+        traffic = None
 
     # CPU baseline: the same six products with PyTorch fp32 on the host cores,
     # on a sample of the rows (the reference has no CPU implementation)
@@ -961,7 +967,7 @@ def run_projections(args, w):
                     for n in names},
         "roofline": {"kernel": dom, "bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1),
                      "unit": "TFLOP/s", "frac": round(achieved / peak, 3), "peak_source": peak_note,
-                     "traffic": None},
+                     "traffic": traffic, "flops_per_launch": flops[dom]},
         "cpu_baseline": {"value": round(cpu_value, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
                          "sample": f"the same six GEMMs on {Bs} of {B} sequences, PyTorch fp32 on the host"},
         "gpu_launches": 6 * args.steps,
