@@ -666,9 +666,10 @@ def run_config4(args, w):
     """The reference NanoGPT architecture (token + position embedding, 6 blocks
     of LayerNorm -> attention -> LayerNorm -> ReLU MLP with no residuals,
     unembedding, softmax, cross-entropy on the probabilities, the reference's
-    Adam) from cudatransformer_b200.nanogpt: the QKV projection, attention and
-    output projection of every block run on this library's tcgen05 kernels,
-    the rest as PyTorch ops (plumbing), fp32.  A step = forward, backward and
+    Adam) from cudatransformer_b200.nanogpt: every block's LayerNorms, QKV
+    projection, attention, output projection and ReLU MLP run on this
+    library's kernels, the embeddings, unembedding, softmax, loss and Adam as
+    PyTorch ops (plumbing), fp32.  A step = forward, backward and
     one Adam update on a fresh batch; steps are stateful, so the warm-up steps
     are part of the training run and the loss of every step is kept.
 
@@ -784,7 +785,8 @@ def run_config4(args, w):
         "warmup": args.warmup,
         "ms_per_step": round(ms, 3),
         "higher_is_better": True,
-        "dtype": "fp32 I/O; attention and its QKV / output projections on tf32 tcgen05 MMA, the rest PyTorch fp32",
+        "dtype": "fp32 I/O; LayerNorm, attention, QKV / output projections and the ReLU MLP on this library "
+                 "(tf32 tcgen05 GEMMs); embeddings, unembedding, softmax, loss and Adam PyTorch fp32",
         "data": "synthetic: weights N(0,0.02) (LayerNorm scale 1, biases 0), token ids uniform [0,65), seeded",
         "config": {"workload": w["desc"], "batch": B, "seq_len": T, "layers": L, "heads": H, "head_dim": D,
                    "causal": w["causal"],

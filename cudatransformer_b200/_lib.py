@@ -71,6 +71,10 @@ SIGNATURES = {
     "ctfa_qkv_backward": (_c_int, [_c_void_p] * 14 + [_c_int] * 6 + [_c_void_p]),
     "ctfa_out_proj_forward": (_c_int, [_c_void_p] * 4 + [_c_int] * 6 + [_c_void_p]),
     "ctfa_out_proj_backward": (_c_int, [_c_void_p] * 6 + [_c_int] * 6 + [_c_void_p]),
+    "ctfa_linear_forward": (_c_int, [_c_void_p] * 4 + [_c_int] * 5 + [_c_void_p]),
+    "ctfa_linear_backward": (_c_int, [_c_void_p] * 7 + [_c_int] * 4 + [_c_void_p]),
+    "ctfa_layernorm_forward": (_c_int, [_c_void_p] * 6 + [_c_int] * 2 + [ctypes.c_float, _c_int, _c_void_p]),
+    "ctfa_layernorm_backward": (_c_int, [_c_void_p] * 8 + [_c_int] * 2 + [ctypes.c_float, _c_int, _c_void_p]),
 }
 
 _lib = None

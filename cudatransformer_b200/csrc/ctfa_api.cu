@@ -840,3 +840,4 @@ extern "C" int ctfa_selftest_wait_timeout(unsigned long long limit_ns, void* str
 }
 
 #include "proj_api.cuh"
+#include "mlp_api.cuh"

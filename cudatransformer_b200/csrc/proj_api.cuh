@@ -62,6 +62,8 @@ struct ProjSimtArgs {
   const void* bias[3];
   void* out[3];
   void* dbias[3];
+  int relu;          // kProjOutFwd: max(y, 0)
+  const void* mask;  // kProjQkvDx: dx *= (mask > 0)
 };
 
 // kind: a ProjKind.  Element counts per kind are computed by the launcher.
@@ -87,7 +89,7 @@ __global__ void __launch_bounds__(256) proj_simt_kernel(int kind, ProjSimtArgs g
       const int o = (int)(idx % E);
       const long long bt = idx / E;
       const int t = (int)(bt % T), b = (int)(bt / T);
-      const int nw = (kind == kProjQkvDx) ? 3 : 1;
+      const int nw = (kind == kProjQkvDx && g.w[1] != nullptr) ? 3 : 1;  // one weight: a Linear layer's dx
       for (int w = 0; w < nw; ++w) {
         const DT* a = static_cast<const DT*>(g.a[w]);
         const DT* wt = static_cast<const DT*>(g.w[w]);
@@ -101,6 +103,8 @@ __global__ void __launch_bounds__(256) proj_simt_kernel(int kind, ProjSimtArgs g
         }
       }
       if (kind == kProjOutFwd && g.bias[0]) acc += pacc(static_cast<const DT*>(g.bias[0])[o]);
+      if (kind == kProjOutFwd && g.relu && !(acc > 0)) acc = 0;
+      if (kind == kProjQkvDx && g.mask && !(pacc(static_cast<const DT*>(g.mask)[idx]) > 0)) acc = 0;
       static_cast<DT*>(g.out[0])[idx] = pout<DT>(acc);
     } else if (kind == kProjOutDa) {  // idx over [B][H][T][D]
       const int d = (int)(idx % D), t = (int)((idx / D) % T), h = (int)((idx / ((long long)D * T)) % H),

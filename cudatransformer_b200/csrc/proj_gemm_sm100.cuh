@@ -57,6 +57,8 @@ struct ProjParams {
   const void* bias[3];  // forward kinds (DT), may be null
   void* dbias[3];       // weight-gradient kinds (DT, accumulated), may be null
   void* dw[3];          // weight-gradient kinds with 16-bit elements: the gradients themselves
+  int relu;             // kProjOutFwd: y = max(y, 0) (a Linear layer followed by ReLU)
+  const void* mask;     // kProjQkvDx: dx *= (mask > 0), mask [B, T, E] (backward of a ReLU before the layer)
   unsigned long long wait_limit_ns;
 };
 
@@ -334,6 +336,20 @@ __global__ void __launch_bounds__(192, STAGES == 2 ? 3 : 2)
           for (int j = 0; j < 32; ++j) {
             const int n = n0 + c * 32 + j;
             v[j] += (n < n_lim) ? proj_to_float(bias[n]) : 0.f;
+          }
+        }
+        if constexpr (KIND == kProjOutFwd) {
+          if (p.relu) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.f);
+          }
+        }
+        if constexpr (KIND == kProjQkvDx) {
+          if (p.mask != nullptr && t0 + r < p.T) {
+            const DT* mrow = static_cast<const DT*>(p.mask) + ((size_t)b * p.T + t0 + r) * p.E + n0 + c * 32;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n0 + c * 32 + j < p.E && !(proj_to_float(mrow[j]) > 0.f)) v[j] = 0.f;
           }
         }
         if constexpr (C::EB == 4) {

@@ -1,7 +1,8 @@
-"""The reference's NanoGPT training step with the whole
-attention layer on this library: QKV projection, attention and output
-projection run as libctfa_b200.so tcgen05 kernels (autograd.py); embedding,
-LayerNorm, the ReLU MLP, unembedding and softmax are PyTorch ops (plumbing).
+"""The reference's NanoGPT training step with every block
+on this library: LayerNorm, QKV projection, attention, output projection and
+the ReLU MLP run as libctfa_b200.so kernels (autograd.py); the embeddings,
+unembedding (vocab 65), softmax, loss and optimizer are PyTorch ops
+(plumbing).
 
 Architecture and optimiser follow the reference (cuda_transformer/):
   * forward, NanoGPT.cu:80-94: token + position embedding -> blocks ->
@@ -23,7 +24,7 @@ from __future__ import annotations
 import numpy as np
 import torch
 
-from .autograd import flash_attention, out_projection, qkv_projection
+from .autograd import flash_attention, layer_norm, mlp, out_projection, qkv_projection
 
 
 def parameter_shapes(layers: int, heads: int, head_dim: int, vocab: int, seq_len: int, mlp: int) -> dict:
@@ -60,19 +61,18 @@ def init_parameters(shapes: dict, seed: int, std: float = 0.02) -> dict:
 def forward(params: dict, ids: torch.Tensor, layers: int, heads: int, head_dim: int, causal: bool) -> torch.Tensor:
     """Softmax probabilities [B, T, vocab]."""
     B, T = ids.shape
-    E = heads * head_dim
     x = params["tokenEmbedding"][ids] + params["positionEmbedding"][:T].unsqueeze(0)
     for i in range(layers):
         p = lambda n: params[f"layer_{i}.{n}"]
-        h = torch.nn.functional.layer_norm(x, (E,), p("firstNorm.weights"), p("firstNorm.biases"), 1e-5)
+        h = layer_norm(x, p("firstNorm.weights"), p("firstNorm.biases"), 1e-5)
         q, k, v = qkv_projection(h, p("attention.query.weights"), p("attention.query.biases"),
                                  p("attention.key.weights"), p("attention.key.biases"),
                                  p("attention.value.weights"), p("attention.value.biases"), heads, head_dim)
         a = out_projection(flash_attention(q, k, v, causal), p("attention.output.weights"),
                            p("attention.output.biases"))
-        h2 = torch.nn.functional.layer_norm(a, (E,), p("secondNorm.weights"), p("secondNorm.biases"), 1e-5)
-        m = torch.relu(h2 @ p("mlp.layer_0.weights").T + p("mlp.layer_0.biases"))
-        x = m @ p("mlp.layer_2.weights").T + p("mlp.layer_2.biases")
+        h2 = layer_norm(a, p("secondNorm.weights"), p("secondNorm.biases"), 1e-5)
+        x = mlp(h2, p("mlp.layer_0.weights"), p("mlp.layer_0.biases"), p("mlp.layer_2.weights"),
+                p("mlp.layer_2.biases"))
     return torch.softmax(x @ params["unEmbedding"].T, -1)
 
 

@@ -240,6 +240,38 @@ int ctfa_out_proj_forward(const void* a, const void* wo, const void* bo, void* y
 int ctfa_out_proj_backward(const void* a, const void* dy, const void* wo, void* dwo, void* dbo, void* da, int B,
                            int T, int E, int H, int D, int dtype, void* stream);
 
+/*
+ * The block's other layers (the config-4 training step): the MLP's Linear
+ * layers and LayerNorm.  Same element types.  Row-major tensors; M rows.
+ */
+/* y [M, N] = x [M, K] W^T + b, W [N, K] (row = output feature, as
+ * cuda_transformer/linear_kernels.cu:64 reads it); relu != 0 applies
+ * max(y, 0) (a ReLU layer after the Linear, relu_kernels.cu:26-38).  Replaces
+ * linearForward (LinearLayer::forward, LinearLayer.cu:55).  b may be NULL.
+ * f32 / bf16 / f16 with K and N multiples of 128 bytes of elements run on the
+ * tensor cores (the projection GEMM with one head), other shapes on SIMT. */
+int ctfa_linear_forward(const void* x, const void* w, const void* b, void* y, int M, int K, int N, int relu, int dtype,
+                        void* stream);
+/* Backward of y = x W^T + b.  Replaces linearBackwardWB + linearBackward
+ * (LinearLayer::backward, LinearLayer.cu:83, :95): dw += dy^T x, db += column
+ * sums of dy (added into the buffers), dx = dy W (overwritten).  dx_mask
+ * (optional, [M, K]): dx is zeroed where dx_mask <= 0 -- the backward of a
+ * ReLU whose output is this layer's input (pass that output, x itself).  dx ==
+ * NULL or dw == db == NULL skip the respective part. */
+int ctfa_linear_backward(const void* x, const void* dy, const void* w, const void* dx_mask, void* dw, void* db,
+                         void* dx, int M, int K, int N, int dtype, void* stream);
+/* y = (x - mean) * rstd * w + b per row of E, biased variance; mean and rstd
+ * (fp32 [M], may be NULL) are kept for the backward.  Replaces
+ * layerNormForwardKernel (LayerNorm.cu:119). */
+int ctfa_layernorm_forward(const void* x, const void* w, const void* b, void* y, float* mean, float* rstd, int M,
+                           int E, float eps, int dtype, void* stream);
+/* dx (overwritten), dw += sum dy * x_hat, db += sum dy (added; either may be
+ * NULL).  Replaces layerNormBackwardKernel (LayerNorm.cu:143).  E <= 1024.
+ * mean / rstd: the forward's (NULL: recomputed from x with eps; double data
+ * always recomputes, the fp32 statistics would cost it precision). */
+int ctfa_layernorm_backward(const void* x, const void* dy, const void* w, const float* mean, const float* rstd,
+                            void* dx, void* dw, void* db, int M, int E, float eps, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
