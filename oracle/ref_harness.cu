@@ -2,7 +2,8 @@
 // FlashAttentionLayer<DType> (cuda_transformer/FlashAttentionLayer.cu, kernels
 // in cuda_transformer/flash_attention.cu), QKVProjectionLayer and
 // OutputProjectionLayer (kernels in attention_qkv_kernels.cu and
-// attention_proj_kernels.cu) unmodified, from the reference tree,
+// attention_proj_kernels.cu), LinearLayer and LayerNormLayer (linear_kernels.cu,
+// layer_norm_kernels.cu) unmodified, from the reference tree,
 // into oracle/_ref/libctref.so, and exposes it through a small C ABI so that
 // tests can compare the reference's CUDA output with libctfa_b200.so and
 // bench.py --impl reference can time the reference's stock code path.
@@ -16,6 +17,8 @@
 // reference's shallow-wrap constructor (Tensor.cu:63).  Nothing of the
 // reference is copied here; the sources are compiled where they lie.
 #include "FlashAttentionLayer.cu"
+#include "LayerNorm.cu"
+#include "LinearLayer.cu"
 #include "OutputProjectionLayer.cu"
 #include "QKVProjectionLayer.cu"
 
@@ -117,7 +120,55 @@ int out_proj(const void* a, const void* wo, const void* bo, void* y, const void*
   return (int)cudaDeviceSynchronize();
 }
 
+// LinearLayer<float>(K, N) (LinearLayer.cu:25) with the caller's weights:
+// forward (:45) and, when dy is given, backward (:73); gradients start at 0.
+int linear(const void* x, const void* w, const void* b, void* y, const void* dy, void* dx, void* dw, void* db, int M,
+           int K, int N) {
+  LinearLayer<float> layer(K, N);
+  layer.weights = borrow<float>(w);
+  layer.biases = borrow<float>(b);
+  Tensor<float> tx(borrow<float>(x), {(size_t)M, (size_t)K});
+  Tensor<float> ty = layer.forward(tx);
+  copy_out<float>(y, ty.dataPtr(), (size_t)M * N);
+  if (dy) {
+    Tensor<float> gx = layer.backward(tx, Tensor<float>(borrow<float>(dy), {(size_t)M, (size_t)N}));
+    copy_out<float>(dx, gx.dataPtr(), (size_t)M * K);
+    copy_out<float>(dw, layer.weightGrad, (size_t)N * K);
+    copy_out<float>(db, layer.biasGrad, (size_t)N);
+  }
+  return (int)cudaDeviceSynchronize();
+}
+
+// LayerNormLayer<float>(E) (LayerNorm.cu:31, eps 1e-5) with the caller's
+// scale / shift: forward (:104) and, when dy is given, backward (:135).
+int layernorm(const void* x, const void* w, const void* b, void* y, const void* dy, void* dx, void* dw, void* db,
+              int M, int E) {
+  LayerNormLayer<float> layer(E);
+  layer.weights = borrow<float>(w);
+  layer.biases = borrow<float>(b);
+  Tensor<float> tx(borrow<float>(x), {(size_t)M, (size_t)E});
+  Tensor<float> ty = layer.forward(tx);
+  copy_out<float>(y, ty.dataPtr(), (size_t)M * E);
+  if (dy) {
+    Tensor<float> gx = layer.backward(tx, Tensor<float>(borrow<float>(dy), {(size_t)M, (size_t)E}));
+    copy_out<float>(dx, gx.dataPtr(), (size_t)M * E);
+    copy_out<float>(dw, layer.weightsGrad, (size_t)E);
+    copy_out<float>(db, layer.biasesGrad, (size_t)E);
+  }
+  return (int)cudaDeviceSynchronize();
+}
+
 }  // namespace
+
+extern "C" int ctref_linear(const void* x, const void* w, const void* b, void* y, const void* dy, void* dx, void* dw,
+                            void* db, int M, int K, int N) {
+  return linear(x, w, b, y, dy, dx, dw, db, M, K, N);
+}
+
+extern "C" int ctref_layernorm(const void* x, const void* w, const void* b, void* y, const void* dy, void* dx,
+                               void* dw, void* db, int M, int E) {
+  return layernorm(x, w, b, y, dy, dx, dw, db, M, E);
+}
 
 // fp32 only.  w/bias/out/grad/dw/db: arrays of 3 device pointers (q, k, v).
 extern "C" int ctref_qkv_projection(const void* x, const void* const* w, const void* const* bias, void* const* out,

@@ -122,3 +122,38 @@ def test_projection_argument_validation(ctfa):
     a = list(obwd)
     a[2] = None  # wo needed for da
     assert ctfa.ctfa_out_proj_backward(*a) == E
+
+
+def test_linear_and_layernorm_argument_validation(ctfa):
+    E = _lib.CTFA_ERR_INVALID_ARGUMENT
+    lf = [FAKE] * 4 + [16, 64, 64, 0, _lib.CTFA_DTYPE_F32, None]
+    for i in (0, 1, 3):  # x, w, y required; b optional
+        a = list(lf)
+        a[i] = None
+        assert ctfa.ctfa_linear_forward(*a) == E
+    for i in (4, 5, 6):
+        a = list(lf)
+        a[i] = 0
+        assert ctfa.ctfa_linear_forward(*a) == E
+    lb = [FAKE] * 7 + [16, 64, 64, _lib.CTFA_DTYPE_F32, None]
+    a = list(lb)
+    a[1] = None  # dy
+    assert ctfa.ctfa_linear_backward(*a) == E
+    a = list(lb)
+    a[0] = None  # x needed for dw
+    assert ctfa.ctfa_linear_backward(*a) == E
+    a = list(lb)
+    a[2] = None  # w needed for dx
+    assert ctfa.ctfa_linear_backward(*a) == E
+    nf = [FAKE] * 6 + [16, 64, 1e-5, _lib.CTFA_DTYPE_F32, None]
+    a = list(nf)
+    a[8] = 0.0  # eps
+    assert ctfa.ctfa_layernorm_forward(*a) == E
+    a = list(nf)
+    a[2] = None  # b
+    assert ctfa.ctfa_layernorm_forward(*a) == E
+    nb = [FAKE] * 8 + [16, 2048, 1e-5, _lib.CTFA_DTYPE_F32, None]
+    assert ctfa.ctfa_layernorm_backward(*nb) == _lib.CTFA_ERR_UNSUPPORTED  # E > 1024
+    nb[9] = 64
+    nb[5] = None  # dx
+    assert ctfa.ctfa_layernorm_backward(*nb) == E

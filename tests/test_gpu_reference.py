@@ -126,3 +126,53 @@ def test_reference_projection_layers_match_oracle_and_library(cuda_device):
     # bias gradients: ours are the true gradient (the restatement)
     for got, want in [*zip(ldb, odb), (ldbo, odbo)]:
         assert po.max_rel_err(n(got), want) < TOL["f32"]
+
+
+@needs_ref
+def test_reference_linear_and_layernorm_match_restatement_and_library(cuda_device):
+    """The reference's own LinearLayer<float> and LayerNormLayer<float>
+    (compiled from its sources) == the float64 restatements (y = x W^T + b,
+    dW/db accumulated from zero, dx; LayerNorm with eps 1e-5), and the
+    library's ctfa_linear_* / ctfa_layernorm_* == the reference within the
+    fp32 tolerances (2e-3 tf32 GEMMs, 1e-5 LayerNorm)."""
+    from cudatransformer_b200 import mlp_layers as ml
+    from oracle import nanogpt_oracle as nano
+    from oracle import projection_oracle as po
+
+    if not hasattr(REF, "ctref_linear"):
+        pytest.skip("libctref.so predates the Linear / LayerNorm entry points; rebuild with make -C oracle ref")
+    M, K, N = 300, 384, 256
+    rng = np.random.default_rng(31)
+    mk = lambda *s, scale=1.0, shift=0.0: torch.tensor(rng.standard_normal(s) * scale + shift, dtype=torch.float32,
+                                                       device=cuda_device)
+    x, w, b, dy = mk(M, K), mk(N, K, scale=K ** -0.5), mk(N, scale=0.1), mk(M, N)
+    y, dx, dw, db = (torch.empty(M, N, device=cuda_device), torch.empty(M, K, device=cuda_device),
+                     torch.empty(N, K, device=cuda_device), torch.empty(N, device=cuda_device))
+    P = lambda t: t.data_ptr()
+    assert REF.ctref_linear(P(x), P(w), P(b), P(y), P(dy), P(dx), P(dw), P(db), M, K, N) == 0
+    n = lambda t: t.detach().double().cpu().numpy()
+    want = {"y": n(x) @ n(w).T + n(b), "dx": n(dy) @ n(w), "dw": n(dy).T @ n(x), "db": n(dy).sum(0)}
+    for name, got in (("y", y), ("dx", dx), ("dw", dw), ("db", db)):
+        assert po.max_rel_err(n(got), want[name]) < 1e-5, name
+    ly = ml.linear_forward(x, w, b)
+    ldw, ldb = torch.zeros_like(w), torch.zeros_like(b)
+    ldx = ml.linear_backward(x, dy, w, dw=ldw, db=ldb)
+    for got, ref in ((ly, y), (ldx, dx), (ldw, dw), (ldb, db)):
+        assert po.max_rel_err(n(got), n(ref)) < TOL["f32"]
+
+    E = 384
+    xl, gl, bl, dyl = mk(M, E, scale=2.0, shift=0.5), mk(E, scale=0.5, shift=1.0), mk(E, scale=0.1), mk(M, E)
+    yl, dxl, dgl, dbl = (torch.empty(M, E, device=cuda_device), torch.empty(M, E, device=cuda_device),
+                         torch.empty(E, device=cuda_device), torch.empty(E, device=cuda_device))
+    assert REF.ctref_layernorm(P(xl), P(gl), P(bl), P(yl), P(dyl), P(dxl), P(dgl), P(dbl), M, E) == 0
+    tx, tg, tb = (torch.tensor(n(t), requires_grad=True) for t in (xl, gl, bl))
+    ry = nano.layer_norm(tx, tg, tb, 1e-5)
+    ry.backward(torch.tensor(n(dyl)))
+    for got, want in ((yl, ry.detach().numpy()), (dxl, tx.grad.numpy()), (dgl, tg.grad.numpy()),
+                      (dbl, tb.grad.numpy())):
+        assert po.max_rel_err(n(got), want) < 1e-5
+    my, mean, rstd = ml.layernorm_forward(xl, gl, bl)
+    mg, mb = torch.zeros_like(gl), torch.zeros_like(bl)
+    mdx = ml.layernorm_backward(xl, dyl, gl, mean, rstd, mg, mb)
+    for got, ref in ((my, yl), (mdx, dxl), (mg, dgl), (mb, dbl)):
+        assert po.max_rel_err(n(got), n(ref)) < 1e-5
