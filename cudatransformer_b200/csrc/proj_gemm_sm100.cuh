@@ -284,6 +284,31 @@ __global__ void __launch_bounds__(192, STAGES == 2 ? 3 : 2)
     const int r = quarter * 32 + lane;
     const uint32_t trow = tbase + ((uint32_t)(quarter * 32) << 16);
     uint8_t* stg = smem;  // staging tile: NBLK column blocks of 128 rows x 128 B
+    // kProjQkvDx with a ReLU mask: fetch this row's 128 mask values while the
+    // MMAs run and keep one bit per column (bit j of keep[c] = column 32c + j).
+    uint32_t keep[4] = {~0u, ~0u, ~0u, ~0u};
+    if constexpr (KIND == kProjQkvDx) {
+      if (p.mask != nullptr && t0 + r < p.T) {
+        const DT* mrow = static_cast<const DT*>(p.mask) + ((size_t)b * p.T + t0 + r) * p.E + n0;
+        if (n0 + 128 <= p.E) {
+          // whole 128-column span; the row start is 16-byte aligned (E * size % 16 == 0)
+          constexpr int PER16 = 16 / C::EB;  // elements per 16-byte load
+#pragma unroll
+          for (int q = 0; q < 128 / PER16; ++q) {
+            const uint4 u = __ldg(reinterpret_cast<const uint4*>(mrow) + q);
+            const DT* e = reinterpret_cast<const DT*>(&u);
+#pragma unroll
+            for (int t = 0; t < PER16; ++t) {
+              const int col = q * PER16 + t;
+              if (!(proj_to_float(e[t]) > 0.f)) keep[col >> 5] &= ~(1u << (col & 31));
+            }
+          }
+        } else {
+          for (int col = 0; col < 128; ++col)
+            if (n0 + col < p.E && !(proj_to_float(mrow[col]) > 0.f)) keep[col >> 5] &= ~(1u << (col & 31));
+        }
+      }
+    }
     bool ok = nk > 0 && mbar_wait(acc_full, 0, abort_flag, limit, 3);
     tc_fence_after();
     if constexpr (C::DW && C::EB == 2) {
@@ -345,11 +370,11 @@ __global__ void __launch_bounds__(192, STAGES == 2 ? 3 : 2)
           }
         }
         if constexpr (KIND == kProjQkvDx) {
-          if (p.mask != nullptr && t0 + r < p.T) {
-            const DT* mrow = static_cast<const DT*>(p.mask) + ((size_t)b * p.T + t0 + r) * p.E + n0 + c * 32;
+          const uint32_t kb = keep[c];
+          if (kb != ~0u) {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-              if (n0 + c * 32 + j < p.E && !(proj_to_float(mrow[j]) > 0.f)) v[j] = 0.f;
+              if (!((kb >> j) & 1u)) v[j] = 0.f;
           }
         }
         if constexpr (C::EB == 4) {

@@ -92,13 +92,25 @@ class ReferenceAdam:
 
     @torch.no_grad()
     def step(self, grads: dict) -> None:
+        """One update of every parameter, as multi-tensor (foreach) ops: a
+        handful of launches for all parameters instead of several per
+        parameter."""
         self.t += 1
         c1, c2 = 1 - self.b1 ** self.t, 1 - self.b2 ** self.t
-        for k, p in self.params.items():
-            g = grads[k]
-            m = self.m[k].mul_(self.b1).add_(g, alpha=1 - self.b1).div_(c1)
-            v = self.v[k].mul_(self.b2).addcmul_(g, g, value=1 - self.b2).div_(c2)
-            p.addcdiv_(m, v.sqrt().add_(self.eps), value=-self.lr)
+        keys = list(self.params)
+        ps = [self.params[k] for k in keys]
+        gs = [grads[k] for k in keys]
+        ms = [self.m[k] for k in keys]
+        vs = [self.v[k] for k in keys]
+        torch._foreach_mul_(ms, self.b1)
+        torch._foreach_add_(ms, gs, alpha=1 - self.b1)
+        torch._foreach_div_(ms, c1)
+        torch._foreach_mul_(vs, self.b2)
+        torch._foreach_addcmul_(vs, gs, gs, value=1 - self.b2)
+        torch._foreach_div_(vs, c2)
+        den = torch._foreach_sqrt(vs)
+        torch._foreach_add_(den, self.eps)
+        torch._foreach_addcdiv_(ps, ms, den, value=-self.lr)
         self.t += 1
 
 

@@ -40,3 +40,24 @@ def test_forward_is_a_distribution():
         p = nano.forward(params, ids, 1, H, D, causal)
         assert p.shape == (3, T, V)
         assert torch.allclose(p.sum(-1), torch.ones(3, T))
+
+
+def test_package_adam_equals_the_restated_reference_adam():
+    """cudatransformer_b200.nanogpt.ReferenceAdam (multi-tensor ops) makes the
+    same updates as the restatement of the reference's Adam
+    (adam_kernels.cu:44-52, AdamOptimizer.cu:74-96), bit for bit in float64."""
+    import torch
+
+    from cudatransformer_b200.nanogpt import ReferenceAdam as PackageAdam
+    from oracle.nanogpt_oracle import ReferenceAdam
+
+    g = torch.Generator().manual_seed(0)
+    p1 = {k: torch.randn(5, 7, generator=g, dtype=torch.float64) for k in "abc"}
+    p2 = {k: v.clone() for k, v in p1.items()}
+    a, r = PackageAdam(p1, lr=1e-2), ReferenceAdam(p2, lr=1e-2)
+    for _ in range(4):
+        grads = {k: torch.randn(5, 7, generator=g, dtype=torch.float64) for k in "abc"}
+        a.step(grads)
+        r.step(grads)
+    assert all(torch.equal(p1[k], p2[k]) for k in "abc")
+    assert a.t == r.t == 8
