@@ -108,6 +108,15 @@ long long sm_count() {
   return sms;
 }
 
+// Opt-in dynamic shared memory per block of the current device (bytes).
+long long max_dynamic_smem() {
+  int dev = 0, bytes = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&bytes, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess || bytes <= 0)
+    return 48 * 1024;
+  return bytes;
+}
+
 // ---------------------------------------------------------------------------
 // Problem description shared by the full-sequence and block entry points.
 // ---------------------------------------------------------------------------

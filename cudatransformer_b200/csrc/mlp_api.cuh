@@ -71,7 +71,7 @@ __global__ void __launch_bounds__(256) layernorm_fwd_kernel(const DT* __restrict
 // Rows are spread over the warps of the grid; each lane keeps partial
 // dw / db for its columns (i = lane + 32 k, k < kMaxCols) in registers, the
 // block reduces them in shared memory and adds one value per column.
-constexpr int kLnMaxCols = 32;  // E <= 1024
+constexpr int kLnMaxCols = 32;  // E <= 1024; wider rows: layernorm_bwd_wide_kernel
 
 template <typename DT>
 __global__ void __launch_bounds__(256) layernorm_bwd_kernel(const DT* __restrict__ x, const DT* __restrict__ dy,
@@ -151,6 +151,79 @@ __global__ void __launch_bounds__(256) layernorm_bwd_kernel(const DT* __restrict
   }
 }
 
+// Rows wider than 32 * kLnMaxCols: the same row math with strided loops;
+// the per-column dw / db partials go straight into the block's shared-memory
+// sums (`smem_red`, 2 E accumulators) or, when those do not fit, into the
+// global gradients.
+template <typename DT>
+__global__ void __launch_bounds__(256) layernorm_bwd_wide_kernel(const DT* __restrict__ x, const DT* __restrict__ dy,
+                                                                 const DT* __restrict__ w,
+                                                                 const float* __restrict__ mean,
+                                                                 const float* __restrict__ rstd, DT* __restrict__ dx,
+                                                                 DT* __restrict__ dw, DT* __restrict__ db, int M, int E,
+                                                                 float eps, int smem_red) {
+  using AT = typename ProjAcc<DT>::type;
+  extern __shared__ unsigned char ln_smem[];
+  AT* red = reinterpret_cast<AT*>(ln_smem);  // [2][E] when smem_red
+  const bool want_p = dw != nullptr || db != nullptr;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if (smem_red) {
+    for (int i = threadIdx.x; i < 2 * E; i += blockDim.x) red[i] = 0;
+    __syncthreads();
+  }
+  const long long warps = (long long)gridDim.x * nw;
+  for (long long row = (long long)blockIdx.x * nw + wid; row < M; row += warps) {
+    const DT* xr = x + row * E;
+    const DT* gr = dy + row * E;
+    AT mu, rs;
+    if (sizeof(AT) == 8 || mean == nullptr || rstd == nullptr) {
+      AT s = 0;
+      for (int i = lane; i < E; i += 32) s += pacc(xr[i]);
+      mu = warp_sum(s) / (AT)E;
+      AT v = 0;
+      for (int i = lane; i < E; i += 32) {
+        const AT d = pacc(xr[i]) - mu;
+        v += d * d;
+      }
+      rs = inv_sqrt(warp_sum(v) / (AT)E + (AT)eps);
+    } else {
+      mu = mean[row];
+      rs = rstd[row];
+    }
+    AT s1 = 0, s2 = 0;
+    for (int i = lane; i < E; i += 32) {
+      const AT xh = (pacc(xr[i]) - mu) * rs;
+      const AT g = pacc(gr[i]);
+      const AT gw = g * pacc(w[i]);
+      s1 += gw;
+      s2 += gw * xh;
+      if (want_p) {
+        if (smem_red) {
+          atomicAdd(&red[i], g * xh);
+          atomicAdd(&red[E + i], g);
+        } else {
+          if (dw) atomicAdd(&dw[i], pout<DT>(g * xh));
+          if (db) atomicAdd(&db[i], pout<DT>(g));
+        }
+      }
+    }
+    s1 = warp_sum(s1) / (AT)E;
+    s2 = warp_sum(s2) / (AT)E;
+    DT* dr = dx + row * E;
+    for (int i = lane; i < E; i += 32) {
+      const AT xh = (pacc(xr[i]) - mu) * rs;
+      dr[i] = pout<DT>(rs * (pacc(gr[i]) * pacc(w[i]) - s1 - xh * s2));
+    }
+  }
+  if (want_p && smem_red) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < E; i += blockDim.x) {
+      if (dw) atomicAdd(&dw[i], pout<DT>(red[i]));
+      if (db) atomicAdd(&db[i], pout<DT>(red[E + i]));
+    }
+  }
+}
+
 template <typename DT>
 int launch_layernorm_fwd(const void* x, const void* w, const void* b, void* y, float* mean, float* rstd, int M, int E,
                          float eps, cudaStream_t st) {
@@ -168,9 +241,22 @@ int launch_layernorm_bwd(const void* x, const void* dy, const void* w, const flo
   using AT = typename ProjAcc<DT>::type;
   const long long blocks = std::max<long long>(1, std::min<long long>((M + 7) / 8, sm_count() * 2));
   const size_t smem = 2 * (size_t)E * sizeof(AT);
-  layernorm_bwd_kernel<DT><<<(unsigned)blocks, 256, smem, st>>>(
-      static_cast<const DT*>(x), static_cast<const DT*>(dy), static_cast<const DT*>(w), mean, rstd,
-      static_cast<DT*>(dx), static_cast<DT*>(dw), static_cast<DT*>(db), M, E, eps);
+  if (E <= 32 * kLnMaxCols) {
+    layernorm_bwd_kernel<DT><<<(unsigned)blocks, 256, smem, st>>>(
+        static_cast<const DT*>(x), static_cast<const DT*>(dy), static_cast<const DT*>(w), mean, rstd,
+        static_cast<DT*>(dx), static_cast<DT*>(dw), static_cast<DT*>(db), M, E, eps);
+  } else {
+    // shared-memory column sums while they fit in the opt-in limit
+    const bool smem_red = smem <= (size_t)max_dynamic_smem();
+    if (smem_red && smem > 48 * 1024) {
+      cudaError_t a = cudaFuncSetAttribute(layernorm_bwd_wide_kernel<DT>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (a != cudaSuccess) return cuda_fail(a, "cudaFuncSetAttribute(layernorm_bwd_wide_kernel)");
+    }
+    layernorm_bwd_wide_kernel<DT><<<(unsigned)blocks, 256, smem_red ? smem : 0, st>>>(
+        static_cast<const DT*>(x), static_cast<const DT*>(dy), static_cast<const DT*>(w), mean, rstd,
+        static_cast<DT*>(dx), static_cast<DT*>(dw), static_cast<DT*>(db), M, E, eps, smem_red ? 1 : 0);
+  }
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? CTFA_OK : cuda_fail(e, "launch layernorm_bwd_kernel");
 }
@@ -309,7 +395,6 @@ extern "C" int ctfa_layernorm_backward(const void* x, const void* dy, const void
   if (s != CTFA_OK) return s;
   if (M <= 0 || E <= 0) return fail(CTFA_ERR_INVALID_ARGUMENT, "M and E must be positive");
   if (!(eps > 0.f)) return fail(CTFA_ERR_INVALID_ARGUMENT, "eps must be positive");
-  if (E > 32 * kLnMaxCols) return fail(CTFA_ERR_UNSUPPORTED, "layernorm backward supports E <= 1024");
   if (!x || !dy || !w || !dx) return fail(CTFA_ERR_INVALID_ARGUMENT, "x, dy, w and dx must be non-null");
   cudaStream_t st = (cudaStream_t)stream;
   switch (dtype) {

@@ -266,7 +266,8 @@ int ctfa_linear_backward(const void* x, const void* dy, const void* w, const voi
 int ctfa_layernorm_forward(const void* x, const void* w, const void* b, void* y, float* mean, float* rstd, int M,
                            int E, float eps, int dtype, void* stream);
 /* dx (overwritten), dw += sum dy * x_hat, db += sum dy (added; either may be
- * NULL).  Replaces layerNormBackwardKernel (LayerNorm.cu:143).  E <= 1024.
+ * NULL).  Replaces layerNormBackwardKernel (LayerNorm.cu:143).  Any E (rows
+ * wider than 1024 take a strided-loop kernel).
  * mean / rstd: the forward's (NULL: recomputed from x with eps; double data
  * always recomputes, the fp32 statistics would cost it precision). */
 int ctfa_layernorm_backward(const void* x, const void* dy, const void* w, const float* mean, const float* rstd,

@@ -1,16 +1,23 @@
 // dropin_check.cu -- TEST INFRASTRUCTURE ONLY.  Compiles the reference's own
 // AttentionLayer / TransformerBlockLayer (cuda_transformer/*.cu, unmodified,
 // from the reference tree) against cudatransformer_b200/FlashAttentionLayer.cu,
-// QKVProjectionLayer.cu and OutputProjectionLayer.cu (the drop-ins),
+// QKVProjectionLayer.cu, OutputProjectionLayer.cu, LinearLayer.cu and
+// LayerNorm.cu (the drop-ins),
 // for every element type the reference instantiates (float, double, half,
 // bfloat16; cuda_transformer.cu:839-842), and exposes one C entry point that
-// runs the reference's AttentionLayer<float>::forward through it.  It proves
-// the drop-in compiles where the reference's layer did, and lets a GPU test
-// compare the composed layer with an fp64 restatement.
+// runs the reference's AttentionLayer<float>::forward through it, another
+// its TransformerBlockLayer<float> forward + backward (whose backward stops
+// at the reference AttentionLayer's released attention output, which the
+// output-projection drop-in rejects).  It proves the drop-ins compile where
+// the reference's layers did, and lets a GPU test compare the composed layer
+// with an fp64 restatement.
 #include "FlashAttentionLayer.cu"  // ours: same include guard as the reference file
 #include "OutputProjectionLayer.cu"  // ours, likewise
 #include "QKVProjectionLayer.cu"  // ours, likewise
+#include "LinearLayer.cu"  // ours, likewise
+#include "LayerNorm.cu"  // ours, likewise
 #include "TransformerBlockLayer.cu"  // reference: pulls AttentionLayer.cu -> our layers
+#include "block_step.cuh"  // g_last_error, dropin_last_error, dropin_block_step
 
 template struct FlashAttentionLayer<float>;
 template struct FlashAttentionLayer<double>;
@@ -24,6 +31,14 @@ template struct OutputProjectionLayer<float>;
 template struct OutputProjectionLayer<double>;
 template struct OutputProjectionLayer<__half>;
 template struct OutputProjectionLayer<__nv_bfloat16>;
+template struct LinearLayer<float>;
+template struct LinearLayer<double>;
+template struct LinearLayer<__half>;
+template struct LinearLayer<__nv_bfloat16>;
+template struct LayerNormLayer<float>;
+template struct LayerNormLayer<double>;
+template struct LayerNormLayer<__half>;
+template struct LayerNormLayer<__nv_bfloat16>;
 template struct AttentionLayer<float>;
 template struct AttentionLayer<__nv_bfloat16>;
 template struct TransformerBlockLayer<float>;
@@ -48,7 +63,8 @@ extern "C" int dropin_attention_forward(const float* x, const float* wq, const f
     Tensor<float> y = layer.forward(load(x, {(size_t)B, (size_t)N, (size_t)E}));
     cudaMemcpy(out, y.data(), y.size() * sizeof(float), cudaMemcpyDeviceToHost);
     return (int)cudaDeviceSynchronize();
-  } catch (const std::exception&) {
+  } catch (const std::exception& e) {
+    g_last_error = e.what();
     return -1;
   }
 }
@@ -74,7 +90,8 @@ extern "C" int dropin_attention_forward_device(const float* x, const float* wq, 
     Tensor<float> out = layer.forward(view(x, {(size_t)B, (size_t)N, (size_t)E}));
     cudaMemcpyAsync(y, out.data(), out.size() * sizeof(float), cudaMemcpyDeviceToDevice, 0);
     return (int)cudaGetLastError();
-  } catch (const std::exception&) {
+  } catch (const std::exception& e) {
+    g_last_error = e.what();
     return -1;
   }
 }

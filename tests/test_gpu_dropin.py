@@ -83,3 +83,150 @@ def test_dropins_do_not_synchronise(cuda_device):
     assert still_running, "the drop-in layer waited for the device"
     ref = reference_fp64(x.astype(np.float64), *(w.astype(np.float64) for w in ws), H, True)
     assert orc.max_rel_err(ty.cpu().numpy(), ref) < 5e-3
+
+
+def _block_names(E, mlp_dim):
+    """getParameters() names and shapes of the reference's
+    TransformerBlockLayer (TransformerBlockLayer.cu getParameters; MLP
+    sub-layers prefixed layer_<i>, MLPLayer.cu:108-117)."""
+    out = {"firstNorm.weights": (E,), "firstNorm.biases": (E,)}
+    for p in ("query", "key", "value"):
+        out[f"attention.{p}.weights"] = (E, E)
+        out[f"attention.{p}.biases"] = (E,)
+    out["attention.output.weights"] = (E, E)
+    out["attention.output.biases"] = (E,)
+    out.update({"secondNorm.weights": (E,), "secondNorm.biases": (E,),
+                "mlp.layer_0.weights": (mlp_dim, E), "mlp.layer_0.biases": (mlp_dim,),
+                "mlp.layer_2.weights": (E, mlp_dim), "mlp.layer_2.biases": (E,)})
+    return out
+
+
+def block_fp64(x, params, H, causal, relu_mask):
+    """fp64 restatement of TransformerBlockLayer::forward
+    (TransformerBlockLayer.cu:60-66: LayerNorm -> attention -> LayerNorm ->
+    Linear, ReLU, Linear; no residual), on torch tensors under autograd.  The
+    ReLU keeps the units `relu_mask` marks (the pattern of the library's own
+    forward: a unit within rounding of zero may switch sides between
+    precisions, which moves its gradient by O(1) and is an error of neither)."""
+    import torch
+    from oracle import nanogpt_oracle as nano
+
+    B, N, E = x.shape
+    D = E // H
+    p = params
+    h = nano.layer_norm(x, p["firstNorm.weights"], p["firstNorm.biases"])
+    heads = lambda t: t.reshape(B, N, H, D).transpose(1, 2)
+    q, k, v = (heads(nano.project(h, p[f"attention.{n}.weights"], p[f"attention.{n}.biases"]))
+               for n in ("query", "key", "value"))
+    o = nano.attention_f64(q, k, v, causal).transpose(1, 2).reshape(B, N, E)
+    a = nano.project(o, p["attention.output.weights"], p["attention.output.biases"])
+    h2 = nano.layer_norm(a, p["secondNorm.weights"], p["secondNorm.biases"])
+    m = nano.project(h2, p["mlp.layer_0.weights"], p["mlp.layer_0.biases"]) * relu_mask
+    return nano.project(m, p["mlp.layer_2.weights"], p["mlp.layer_2.biases"])
+
+
+BLOCK_LIB = orc.HERE / "_ref" / "libct_dropin_block.so"
+
+
+def _block_inputs(B, N, E, mlp_dim):
+    rng = np.random.default_rng(B * N + E + mlp_dim)
+    shapes = _block_names(E, mlp_dim)
+    params = {}
+    for name, shp in shapes.items():
+        if name.endswith("Norm.weights"):
+            params[name] = (1.0 + 0.2 * rng.standard_normal(shp)).astype(np.float32)
+        elif name.endswith("biases"):
+            params[name] = (0.1 * rng.standard_normal(shp)).astype(np.float32)
+        else:
+            params[name] = (rng.standard_normal(shp) / np.sqrt(shp[1])).astype(np.float32)
+    x = rng.standard_normal((B, N, E)).astype(np.float32)
+    dy = rng.standard_normal((B, N, E)).astype(np.float32)
+    return params, x, dy
+
+
+def _run_block(path, params, x, dy, H, mlp_dim, causal):
+    """dropin_block_step of the harness at `path`: (rc, message, y, dx,
+    hidden, grads, held) -- held: the parameters the block held after its
+    setParameters(params)."""
+    lib = ctypes.CDLL(str(path))
+    fp = ctypes.POINTER(ctypes.c_float)
+    I = ctypes.c_int
+    lib.dropin_block_step.argtypes = [fp] * 4 + [I] * 7 + [ctypes.POINTER(ctypes.c_char_p),
+                                                           ctypes.POINTER(fp), ctypes.POINTER(fp),
+                                                           ctypes.POINTER(ctypes.c_longlong), fp]
+    lib.dropin_block_step.restype = I
+    lib.dropin_last_error.restype = ctypes.c_char_p
+    B, N, E = x.shape
+    y, dx = np.empty_like(x), np.empty_like(x)
+    hidden = np.empty((B, N, mlp_dim), dtype=np.float32)
+    names = list(params)
+    held = {k: v.copy() for k, v in params.items()}
+    grads = {n: np.empty_like(params[n]) for n in names}
+    ptr = lambda a: a.ctypes.data_as(fp)
+    n = len(names)
+    rc = lib.dropin_block_step(ptr(x), ptr(dy), ptr(y), ptr(dx), B, N, E, H, mlp_dim, int(causal), n,
+                               (ctypes.c_char_p * n)(*(s.encode() for s in names)),
+                               (fp * n)(*(ptr(held[s]) for s in names)), (fp * n)(*(ptr(grads[s]) for s in names)),
+                               (ctypes.c_longlong * n)(*(params[s].size for s in names)), ptr(hidden))
+    return rc, lib.dropin_last_error().decode(), y, dx, hidden, grads, held
+
+
+@pytest.mark.skipif(not BLOCK_LIB.exists(), reason="oracle/_ref/libct_dropin_block.so not built (needs the reference tree)")
+@pytest.mark.parametrize("B,N,E,H,mlp_dim,causal", [(2, 128, 256, 4, 512, True), (1, 192, 256, 4, 256, False)])
+def test_reference_transformer_block_with_dropins(cuda_device, B, N, E, H, mlp_dim, causal):
+    """The reference's TransformerBlockLayer<float> forward + backward with
+    every sub-layer it builds from a drop-in (LayerNorm, the F3-fixed
+    AttentionLayer over the projection and flash-attention drop-ins, the MLP's
+    Linear layers; the ReLU is the reference's): y, dx and all 16 parameter
+    gradients against fp64 autograd of the same block, at 1e-2
+    (max|x - x64| / max|x64|; about seven tf32 GEMM / attention stages in a
+    row, each held to 2e-3 by its own tests).  The key-bias gradient is zero
+    in exact arithmetic (softmax is shift invariant), so it is held to the
+    query-bias gradient's scale.  getGradients() must list the LayerNorm
+    gradients, which the reference's LayerNorm lacks.
+
+    The block's setParameters() keeps every parameter given except the
+    second LayerNorm's, which stay at their initial scale 1 / shift 0: it
+    strips 12 characters from the 11-character prefix "secondNorm."
+    (TransformerBlockLayer.cu:159).  The fp64 side uses the parameters the
+    block held."""
+    import torch
+
+    params, x, dy = _block_inputs(B, N, E, mlp_dim)
+    rc, msg, y, dx, hidden, grads, held = _run_block(BLOCK_LIB, params, x, dy, H, mlp_dim, causal)
+    assert rc != -2, "getGradients() lacks a parameter getParameters() lists"
+    assert rc == 0, msg
+    for name in params:
+        if name.startswith("secondNorm."):
+            assert np.array_equal(held[name], np.full_like(params[name], name.endswith("weights")))
+        else:
+            assert np.array_equal(held[name], params[name]), name
+
+    tp = {k: torch.tensor(v, dtype=torch.float64, requires_grad=True) for k, v in held.items()}
+    tx = torch.tensor(x, dtype=torch.float64, requires_grad=True)
+    ty = block_fp64(tx, tp, H, causal, torch.tensor(hidden > 0))
+    ty.backward(torch.tensor(dy, dtype=torch.float64))
+    tol = 1e-2
+    errs = {"y": orc.max_rel_err(y, ty.detach().numpy()), "dx": orc.max_rel_err(dx, tx.grad.numpy())}
+    for name in params:
+        ref = tp[name].grad.numpy()
+        if name == "attention.key.biases":
+            errs[name] = np.abs(grads[name] - ref).max() / np.abs(tp["attention.query.biases"].grad.numpy()).max()
+        else:
+            errs[name] = orc.max_rel_err(grads[name], ref)
+    bad = {k: v for k, v in errs.items() if not v < tol}
+    assert not bad, bad
+
+
+@needs_lib
+def test_reference_attention_layer_backward_stops_at_released_output(cuda_device):
+    """F3 in place: the same block with the reference's own AttentionLayer
+    (libct_dropin.so) runs its forward, and its backward hands the output
+    projection the attention output that AttentionLayer::forward released
+    (AttentionLayer.cu:88-100, :136).  The output-projection drop-in rejects
+    the empty tensor on the host, before any launch (the reference's own
+    layer divides by its zero sequence length, OutputProjectionLayer.cu:76-77)."""
+    params, x, dy = _block_inputs(1, 128, 256, 256)
+    rc, msg, *_ = _run_block(LIB, params, x, dy, 4, 256, True)
+    assert rc == -1
+    assert "OutputProjectionLayer" in msg, msg

@@ -62,7 +62,9 @@ def test_linear_matches_restatement(cuda_device, shape, dt, relu):
     torch.cuda.synchronize()
 
 
-@pytest.mark.parametrize("ME", [(777, 384), (64, 1000), (5, 33)])
+# (40, 3000), (4, 12000), (3, 30000): rows wider than 1024 -- column sums in
+# shared memory, in opt-in shared memory, and straight into global memory
+@pytest.mark.parametrize("ME", [(777, 384), (64, 1000), (5, 33), (40, 3000), (4, 12000), (3, 30000)])
 @pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16, torch.float64])
 def test_layernorm_matches_restatement(cuda_device, ME, dt):
     from cudatransformer_b200 import mlp_layers as ml
