@@ -554,15 +554,18 @@ __global__ void __launch_bounds__(320, 1)
     const uint32_t aK = smem_u32(sK), aV = smem_u32(sV);
     // S^T = K Q^T, dP^T = V dO^T: A is the 128-key tile, B the streamed query tile.
     auto gemm_ss = [&](uint32_t d, uint32_t a_tile, uint32_t b_tile) {
+      const uint64_t a0 = kmajor_desc(a_tile, 128, 0), b0 = kmajor_desc(b_tile, QT, 0);
 #pragma unroll
       for (int ks = 0; ks < C::KSTEP_S; ++ks)
-        umma_ss<kKind>(d, kmajor_desc(a_tile, 128, ks), kmajor_desc(b_tile, QT, ks), idesc_s, ks > 0 ? 1u : 0u);
+        umma_ss<kKind>(d, desc_advance(a0, kmajor_offset(128, ks)), desc_advance(b0, kmajor_offset(QT, ks)), idesc_s,
+                       ks > 0 ? 1u : 0u);
     };
     // dV += P^T dO, dK += dS^T Q: A from TMEM, B = MN-major query tile.
     auto gemm_ts = [&](uint32_t d, uint32_t a_base, uint32_t b_tile, bool acc) {
+      const uint64_t b0 = mnmajor_desc<C::TF32>(b_tile, QT, 0, C::K_PER);
 #pragma unroll
       for (int ks = 0; ks < QT / C::K_PER; ++ks)
-        umma_ts<kKind>(d, a_base + C::a_col(ks, HALF), mnmajor_desc<C::TF32>(b_tile, QT, ks, C::K_PER), idesc_t,
+        umma_ts<kKind>(d, a_base + C::a_col(ks, HALF), desc_advance(b0, mnmajor_offset(ks, C::K_PER)), idesc_t,
                        (acc || ks > 0) ? 1u : 0u);
     };
     int g = 0, ni = 0;
@@ -590,15 +593,26 @@ __global__ void __launch_bounds__(320, 1)
       for (int it = 0; it < n_it; ++it, ++g) {
         const int st = g % ST;
         const int st1 = (g + 1) % ST;
-        if (it + 1 < n_it) {
-          if (!(ok = mbar_wait_warp(s_free, g & 1, abort_flag, limit, 14))) break;
-          if (!(ok = mbar_wait_warp(&q_full[st1], ((g + 1) / ST) & 1, abort_flag, limit, 15))) break;
-          tc_fence_after();
-          if (elect_one()) {
-            gemm_ss(tbase + C::KV_S, aK, smem_u32(sQ(st1)));
-            umma_commit(s_full);
+        // S^T of the next query tile.  With early P^T (tf32) it is queued after
+        // dV of this tile: dV only waits for the exponentials, while the next
+        // tile's Q / dO stage is refilled only once dK of the tile before this
+        // one has run, so issuing S^T first would park the MMA warp on that
+        // load with dV ready behind it.
+        auto issue_next_s = [&]() -> bool {
+          if (it + 1 < n_it) {
+            if (!mbar_wait_warp(s_free, g & 1, abort_flag, limit, 14)) return false;
+            if (!mbar_wait_warp(&q_full[st1], ((g + 1) / ST) & 1, abort_flag, limit, 15)) return false;
+            tc_fence_after();
+            if (elect_one()) {
+              gemm_ss(tbase + C::KV_S, aK, smem_u32(sQ(st1)));
+              umma_commit(s_full);
+            }
+            __syncwarp();
           }
-          __syncwarp();
+          return true;
+        };
+        if constexpr (!C::EARLY_P) {
+          if (!(ok = issue_next_s())) break;
         }
         if constexpr (C::EARLY_P) {
           // dV (+)= P^T dO as soon as P^T is stored, while dS^T is formed
@@ -608,6 +622,7 @@ __global__ void __launch_bounds__(320, 1)
           tc_fence_after();
           if (elect_one()) gemm_ts(tbase + C::KV_DV, tbase + C::kv_p(g & 1), smem_u32(sdOm(st)), it > 0);
           __syncwarp();
+          if (!(ok = issue_next_s())) break;
         }
         if (!(ok = mbar_wait_warp(p_full, g & 1, abort_flag, limit, 16))) break;
         if (!C::EARLY_P && it == 0 && ni > 0 && !(ok = mbar_wait_warp(acc_free, (ni - 1) & 1, abort_flag, limit, 34)))
@@ -934,17 +949,19 @@ __global__ void __launch_bounds__(320, 1)
     const uint32_t aQ = smem_u32(sQ), adO = smem_u32(sdO);
     // S = Q K^T, dP = dO V^T: A is the 128-query tile, B the streamed key tile.
     auto gemm_ss = [&](uint32_t d, uint32_t a_tile, uint32_t b_tile) {
+      const uint64_t a0 = kmajor_desc(a_tile, 128, 0), b0 = kmajor_desc(b_tile, KT, 0);
 #pragma unroll
       for (int ks = 0; ks < C::KSTEP_S; ++ks)
-        umma_ss<kKind>(d, kmajor_desc(a_tile, 128, ks), kmajor_desc(b_tile, KT, ks), idesc_s, ks > 0 ? 1u : 0u);
+        umma_ss<kKind>(d, desc_advance(a0, kmajor_offset(128, ks)), desc_advance(b0, kmajor_offset(KT, ks)), idesc_s,
+                       ks > 0 ? 1u : 0u);
     };
     // dQ (+)= dS K: A = dS from TMEM, B = the key tile read MN-major.
     auto gemm_dq = [&](int st, bool acc) {
-      const uint32_t bK = smem_u32(sKm(st));
+      const uint64_t b0 = mnmajor_desc<C::TF32>(smem_u32(sKm(st)), KT, 0, C::K_PER);
 #pragma unroll
       for (int ks = 0; ks < KT / C::K_PER; ++ks)
         umma_ts<kKind>(tbase + C::Q_DQ, tbase + C::q_dp(0) + C::a_col(ks, HALF),
-                       mnmajor_desc<C::TF32>(bK, KT, ks, C::K_PER), idesc_t, (acc || ks > 0) ? 1u : 0u);
+                       desc_advance(b0, mnmajor_offset(ks, C::K_PER)), idesc_t, (acc || ks > 0) ? 1u : 0u);
     };
     int g = 0, ni = 0;
     bool ok = true;

@@ -77,12 +77,22 @@ struct FwdConfig {
   // NQ softmax warpgroups + one producer warpgroup (TMA warp, MMA warp, two
   // spare warps) so that registers can be rebalanced per warpgroup.
   static constexpr int THREADS = NQ * 128 + 128;
-  // With NQ = 2 the block launches at 168 registers/thread (3 warps per SMSP):
-  // 384 * 168 = 64512 = 256 * 224 (softmax) + 128 * 56 (producer).
-  static constexpr bool REBALANCE = (NQ == 2);
-  static constexpr int SOFTMAX_REGS = 224;
+  // The block launches at LAUNCH_REGS registers/thread (the launch bound's
+  // share of the 64 K register file, in the allocator's steps of 8); the
+  // producer warpgroup drops to 56 and the softmax warpgroups take the rest:
+  // NQ = 2: 384 * 168 = 64512 >= 256 * 224 + 128 * 56;
+  // NQ = 3: 512 * 128 = 65536 >= 384 * 152 + 128 * 56;
+  // NQ = 4: 640 * 96 = 61440 >= 512 * 104 + 128 * 56.
+  // The host checks the compiled register count against LAUNCH_REGS before
+  // the first launch (a split above the launch's registers would never be
+  // granted).
+  static constexpr int LAUNCH_REGS = (65536 / THREADS) / 8 * 8 > 255 ? 248 : (65536 / THREADS) / 8 * 8;
+  static constexpr bool REBALANCE = (NQ >= 2);
   static constexpr int PRODUCER_REGS = 56;
-  static_assert(!REBALANCE || 256 * SOFTMAX_REGS + 128 * PRODUCER_REGS <= 384 * 168, "register split");
+  static constexpr int SOFTMAX_REGS_RAW = (LAUNCH_REGS * THREADS - 128 * PRODUCER_REGS) / (NQ * 128) / 8 * 8;
+  static constexpr int SOFTMAX_REGS = SOFTMAX_REGS_RAW > 248 ? 248 : SOFTMAX_REGS_RAW;
+  static_assert(!REBALANCE || NQ * 128 * SOFTMAX_REGS + 128 * PRODUCER_REGS <= THREADS * LAUNCH_REGS,
+                "register split");
   static_assert(HD * EB % 128 == 0, "head dim must fill whole 128-byte rows");
   static_assert(BN % 32 == 0 && BN <= 256, "key tile");
   static_assert(NQ * (BN + HD) <= 512, "TMEM budget");
@@ -263,21 +273,20 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
 
       auto issue_s = [&](int k, int st) {
         const uint32_t d = tbase + k * BN;
+        const uint64_t a0 = kmajor_desc(sQ_addr + k * C::Q_TILE_BYTES, BM, 0);
+        const uint64_t b0 = kmajor_desc(sK_addr + st * C::KV_TILE_BYTES, BN, 0);
 #pragma unroll
-        for (int ks = 0; ks < C::KSTEP_S; ++ks) {
-          const uint64_t a = kmajor_desc(sQ_addr + k * C::Q_TILE_BYTES, BM, ks);
-          const uint64_t b = kmajor_desc(sK_addr + st * C::KV_TILE_BYTES, BN, ks);
-          umma_ss<kKind>(d, a, b, idesc_s, ks > 0 ? 1u : 0u);
-        }
+        for (int ks = 0; ks < C::KSTEP_S; ++ks)
+          umma_ss<kKind>(d, desc_advance(a0, kmajor_offset(BM, ks)), desc_advance(b0, kmajor_offset(BN, ks)), idesc_s,
+                         ks > 0 ? 1u : 0u);
       };
       auto issue_pv = [&](int k, int st, bool acc) {
         const uint32_t d = tbase + NQ * BN + k * HD;
+        const uint64_t b0 = mnmajor_desc<C::EB == 4>(sV_addr + st * C::KV_TILE_BYTES, BN, 0, C::K_PER_PV);
 #pragma unroll
-        for (int ks = 0; ks < C::KSTEP_PV; ++ks) {
-          const uint32_t a = tbase + k * BN + ks * 8;
-          const uint64_t b = mnmajor_desc<C::EB == 4>(sV_addr + st * C::KV_TILE_BYTES, BN, ks, C::K_PER_PV);
-          umma_ts<kKind>(d, a, b, idesc_pv, (acc || ks > 0) ? 1u : 0u);
-        }
+        for (int ks = 0; ks < C::KSTEP_PV; ++ks)
+          umma_ts<kKind>(d, tbase + k * BN + ks * 8, desc_advance(b0, mnmajor_offset(ks, C::K_PER_PV)), idesc_pv,
+                         (acc || ks > 0) ? 1u : 0u);
       };
 
       bool ok = mbar_wait_warp(q_go, 0, abort_flag, limit, 3);

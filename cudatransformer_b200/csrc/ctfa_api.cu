@@ -176,6 +176,17 @@ int launch_fwd_tc(const Problem& pr, const void* q, const void* k, const void* v
   auto kern = attn_fwd_sm100<DT, HD, NQ, BN, KST, VST, RND>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attn_fwd_sm100)");
+  if constexpr (C::REBALANCE) {
+    // setmaxnreg can only redistribute the registers the block launched with
+    static int checked_regs = 0;
+    if (checked_regs == 0) {
+      cudaFuncAttributes fa;
+      if ((e = cudaFuncGetAttributes(&fa, kern)) != cudaSuccess) return cuda_fail(e, "cudaFuncGetAttributes");
+      checked_regs = fa.numRegs;
+    }
+    if (checked_regs < C::LAUNCH_REGS)
+      return fail(CTFA_ERR_UNSUPPORTED, "attn_fwd_sm100 compiled below its register split");
+  }
   const long long grid = (long long)p.n_groups * p.BH;
   if (grid > 0x7fffffffLL) return fail(CTFA_ERR_UNSUPPORTED, "grid too large");
   kern<<<(unsigned)grid, C::THREADS, C::SMEM_BYTES, stream>>>(mq, mk, mv, mqr, mkr, mvr, p);

@@ -260,10 +260,12 @@ __global__ void __launch_bounds__(192, STAGES == 2 ? 3 : 2)
       if (elect_one()) {
         const uint32_t sa = sbase + s * C::STAGE_BYTES;
         const uint32_t sb = sa + C::TILE_BYTES;
+        const uint64_t a0 = C::A_MN ? mnmajor_desc<kTF32>(sa, KB, 0, C::K_PER_MMA) : kmajor_desc(sa, 128, 0);
+        const uint64_t b0 = C::B_MN ? mnmajor_desc<kTF32>(sb, KB, 0, C::K_PER_MMA) : kmajor_desc(sb, 128, 0);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t ad = C::A_MN ? mnmajor_desc<kTF32>(sa, KB, kk, C::K_PER_MMA) : kmajor_desc(sa, 128, kk);
-          const uint64_t bd = C::B_MN ? mnmajor_desc<kTF32>(sb, KB, kk, C::K_PER_MMA) : kmajor_desc(sb, 128, kk);
+          const uint64_t ad = desc_advance(a0, C::A_MN ? mnmajor_offset(kk, C::K_PER_MMA) : kmajor_offset(128, kk));
+          const uint64_t bd = desc_advance(b0, C::B_MN ? mnmajor_offset(kk, C::K_PER_MMA) : kmajor_offset(128, kk));
           umma_ss<kKind>(tbase, ad, bd, idesc, (i > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&empty[s]);

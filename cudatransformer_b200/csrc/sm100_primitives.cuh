@@ -299,6 +299,21 @@ __device__ __forceinline__ uint64_t mnmajor_desc(uint32_t tile_addr, int red_row
                     kTF32 ? kLayoutSW128Base32 : kLayoutSW128);
 }
 
+// k-step offsets (bytes from the tile start) of the two layouts above, and a
+// descriptor advanced by such an offset: the start-address field holds the
+// address in 16-byte units in bits 0..13, and shared-memory addresses stay
+// below 256 KB, so adding offset/16 to the k-step-0 descriptor gives the
+// k-step's descriptor without a carry into the other fields.  The MMA-issuing
+// thread then spends one add per operand and k-step instead of rebuilding the
+// descriptor.
+__host__ __device__ constexpr uint32_t kmajor_offset(int rows, int ks) {
+  return (uint32_t)((ks >> 2) * (rows * 128) + (ks & 3) * 32);
+}
+__host__ __device__ constexpr uint32_t mnmajor_offset(int ks, int k_per) { return (uint32_t)(ks * k_per * 128); }
+__device__ __forceinline__ uint64_t desc_advance(uint64_t desc0, uint32_t offset_bytes) {
+  return desc0 + (uint64_t)(offset_bytes >> 4);
+}
+
 // Instruction descriptor for kind::f16 / kind::tf32 with fp32 accumulation.
 //   fmt: 0 = f16, 1 = bf16, 2 = tf32.  b_mn_major: B operand stored N-contiguous.
 __host__ __device__ constexpr uint32_t make_idesc(uint32_t fmt, int M, int N, bool a_mn_major, bool b_mn_major) {
