@@ -598,9 +598,9 @@ __global__ void __launch_bounds__(320, 1)
         // tile's Q / dO stage is refilled only once dK of the tile before this
         // one has run, so issuing S^T first would park the MMA warp on that
         // load with dV ready behind it.
-        auto issue_next_s = [&]() -> bool {
+        auto issue_next_s = [&](bool wait_s_free) -> bool {
           if (it + 1 < n_it) {
-            if (!mbar_wait_warp(s_free, g & 1, abort_flag, limit, 14)) return false;
+            if (wait_s_free && !mbar_wait_warp(s_free, g & 1, abort_flag, limit, 14)) return false;
             if (!mbar_wait_warp(&q_full[st1], ((g + 1) / ST) & 1, abort_flag, limit, 15)) return false;
             tc_fence_after();
             if (elect_one()) {
@@ -612,7 +612,7 @@ __global__ void __launch_bounds__(320, 1)
           return true;
         };
         if constexpr (!C::EARLY_P) {
-          if (!(ok = issue_next_s())) break;
+          if (!(ok = issue_next_s(true))) break;
         }
         if constexpr (C::EARLY_P) {
           // dV (+)= P^T dO as soon as P^T is stored, while dS^T is formed
@@ -622,7 +622,9 @@ __global__ void __launch_bounds__(320, 1)
           tc_fence_after();
           if (elect_one()) gemm_ts(tbase + C::KV_DV, tbase + C::kv_p(g & 1), smem_u32(sdOm(st)), it > 0);
           __syncwarp();
-          if (!(ok = issue_next_s())) break;
+          // every compute thread arrives on s_free (S^T read) before pt_full,
+          // so the completed pt_full phase implies the s_free one
+          if (!(ok = issue_next_s(false))) break;
         }
         if (!(ok = mbar_wait_warp(p_full, g & 1, abort_flag, limit, 16))) break;
         if (!C::EARLY_P && it == 0 && ni > 0 && !(ok = mbar_wait_warp(acc_free, (ni - 1) & 1, abort_flag, limit, 34)))
