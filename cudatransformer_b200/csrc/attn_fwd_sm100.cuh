@@ -355,15 +355,23 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
     // Round a landed tile in place and make the writes visible to the async
     // proxy (tcgen05.mma, TMA store); the caller then arrives on the tile's
     // ready barrier (64 arrivals), which the MMA warp and the storing lane wait on.
+    // Tiles are whole multiples of 256 16-byte vectors: four loads in flight
+    // per thread.
+    static_assert(C::Q_TILE_BYTES % (64 * 64) == 0 && C::KV_TILE_BYTES % (64 * 64) == 0, "rounding split");
     auto round_tile = [&](uint8_t* tile, int bytes) {
       float4* t4 = reinterpret_cast<float4*>(tile);
-      for (int i = sub; i < bytes / 16; i += 64) {
-        float4 x = t4[i];
-        x.x = __uint_as_float(f32_to_tf32_rna(x.x));
-        x.y = __uint_as_float(f32_to_tf32_rna(x.y));
-        x.z = __uint_as_float(f32_to_tf32_rna(x.z));
-        x.w = __uint_as_float(f32_to_tf32_rna(x.w));
-        t4[i] = x;
+      for (int i = sub; i < bytes / 16; i += 4 * 64) {
+        float4 x[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) x[u] = t4[i + u * 64];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          x[u].x = __uint_as_float(f32_to_tf32_rna(x[u].x));
+          x[u].y = __uint_as_float(f32_to_tf32_rna(x[u].y));
+          x[u].z = __uint_as_float(f32_to_tf32_rna(x[u].z));
+          x[u].w = __uint_as_float(f32_to_tf32_rna(x[u].w));
+          t4[i + u * 64] = x[u];
+        }
       }
       fence_proxy_async_smem();
     };
