@@ -437,9 +437,11 @@ def run_ours(args, w):
         _lib.check(lib.ctfa_backward(bq, bk, bv, oo, doi, lse.data_ptr(), dqo, dko, dvo, bws.data_ptr(), bws.numel(),
                                      B, H, T, D, bcode, causal, sh), "ctfa_backward")
 
-    def e2e_run(steps):
+    def e2e_run(steps, compute=True):
         """Runs `steps` end-to-end steps; returns the device time from the
-        first step's first H2D copy to the last step's last D2H copy."""
+        first step's first H2D copy to the last step's last D2H copy.
+        compute=False: the same copies with no kernels between them (the
+        PCIe floor of the pipeline; reported beside the e2e number)."""
         torch.cuda.synchronize(dev)
         s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s_ev.record(h2d_s)
@@ -454,7 +456,8 @@ def run_ours(args, w):
             stream.wait_event(st["ev_in"])
             if i >= 2:
                 stream.wait_event(st["ev_out"])  # step i-2's outputs have left the device
-            e2e_compute(st)
+            if compute:
+                e2e_compute(st)
             st["ev_comp"].record(stream)
             with torch.cuda.stream(d2h_s):
                 d2h_s.wait_event(st["ev_comp"])
@@ -488,6 +491,8 @@ def run_ours(args, w):
     e2e_run(args.warmup)
     barrier(world)
     ms_e2e = max_over_ranks(e2e_run(args.steps), world)
+    barrier(world)
+    ms_copies = max_over_ranks(e2e_run(args.steps, compute=False), world)
     barrier(world)
 
     # per-kernel durations (events recorded on the launch stream around each launch)
@@ -568,7 +573,10 @@ def run_ours(args, w):
         "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": 4 * nbytes,
                 "d2h_bytes_per_step": 4 * nbytes, "ms_per_step": round(ms_e2e / args.steps, 4),
                 "path": "ctfa_forward + ctfa_backward (C ABI) with pinned host buffers; each step's H2D and D2H "
-                        "copies run on their own streams, overlapping the neighbouring steps' compute"},
+                        "copies run on their own streams, overlapping the neighbouring steps' compute",
+                "copies_only_ms_per_step": round(ms_copies / args.steps, 4),
+                "of_copy_floor": round(ms_copies / ms_e2e, 3),
+                "copy_floor_gbs_per_direction": round(4 * nbytes / (ms_copies / args.steps * 1e-3) / 1e9, 1)},
         "gpu_launches": (5 if fws_bytes else 4) * args.steps,
         "roofline": {"kernel": dom, "bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1),
                      "unit": "TFLOP/s", "frac": round(achieved / peak, 3) if peak else None,
