@@ -175,9 +175,12 @@ struct BwdConfig {
   static constexpr int KSTEP_S = HD * EB / 32;        // k-steps over the head dim (32 bytes each)
   static constexpr int K_PER = TF32 ? 8 : 16;         // reduction rows per TS MMA
   static constexpr int ROW_BYTES = HD * EB;
-  // dK/dV kernel: 128 stationary keys (MMA M); streamed query tiles of KV_QT rows.
+  // dK/dV kernel: 128 stationary keys (MMA M); streamed query tiles of KV_QT
+  // rows.  128 for every type: the S^T / dP^T MMAs are then N=128 (twice the
+  // work of an N=64 MMA for ~1.35x its time; the MMA-issuing warp, which
+  // bounds this kernel, issues 25 % fewer MMAs and half the waits per query).
   static constexpr int KV_KEYS = 128;
-  static constexpr int KV_QT = TF32 ? 64 : 128;
+  static constexpr int KV_QT = 128;
   // dQ kernel: 128 stationary queries; streamed key tiles of Q_KT rows (128:
   // N=128 MMAs run at ~1.7x the per-MAC rate of N=64 ones, and the per-tile
   // barrier / TMEM round trips are amortised over twice the keys).
@@ -189,6 +192,12 @@ struct BwdConfig {
   static constexpr int KV_QTILE = KV_QT * ROW_BYTES;
   static constexpr int Q_KTILE = Q_KT * ROW_BYTES;
   static constexpr int KV_STAGE_BYTES = (TF32 ? 4 : 2) * KV_QTILE;  // Q, dO (+ MN copies)
+  // A stage's query tiles are released in KV_PARTS groups, each after its
+  // last reader: tf32 (one stage fits) Q after S^T, dO after dP^T, the dO MN
+  // copy after dV, the Q MN copy after dK, so every tile of the next query
+  // tile loads while the current one is still in use; 16-bit (2-3 stages)
+  // releases Q and dO together after dK.
+  static constexpr int KV_PARTS = TF32 ? 4 : 1;
   static constexpr int Q_KSTAGE_BYTES = (TF32 ? 2 : 1) * Q_KTILE;   // K (+ K MN copy)
   static constexpr int Q_VSTAGE_BYTES = Q_KTILE;                    // V
   static constexpr int BUDGET = 216 * 1024;
@@ -202,9 +211,11 @@ struct BwdConfig {
   static constexpr int Q_VST = TF32 ? 1 : Q_KST;
   // dK/dV kernel TMEM map (columns, lanes = keys).  S^T, then the dP^T buffer
   // (dS^T after the compute pass: tf32 in place; 16-bit: dS^T|P^T packed per
-  // half), then for tf32 two P^T buffers (EARLY_P: the compute warps store P^T
+  // half), then for tf32 the P^T buffer (EARLY_P: the compute warps store P^T
   // right after the exponentials and release it, so dV (+)= P^T dO runs while
-  // they form dS^T; only dK waits for dS^T), then the dK and dV accumulators.
+  // they form dS^T; only dK waits for dS^T; P^T of tile g overwrites that of
+  // tile g-1 once S^T of tile g completed, which dV of tile g-1 precedes in
+  // the MMA stream), then the dK and dV accumulators.
   // A second dP^T buffer (so the next dP^T GEMM is queued before the compute
   // warps release the current one) measured 4-8% slower: thread-side TMEM
   // loads/stores take ~4x longer while the tensor pipe is busy.
@@ -212,11 +223,11 @@ struct BwdConfig {
   static constexpr bool EARLY_P = TF32;
   static constexpr int KV_S = 0;
   static constexpr int KV_DP = KV_QT;
-  static constexpr int KV_DK = TF32 ? 4 * KV_QT : 2 * KV_QT;
+  static constexpr int KV_DK = TF32 ? 3 * KV_QT : 2 * KV_QT;
   static constexpr int KV_DV = KV_DK + HD;
   static constexpr uint32_t KV_TMEM = tmem_cols_for(KV_DV + HD);
-  // P^T of tile g: tf32 buffer g % 2; 16-bit: packed into the dP^T buffer
-  __host__ __device__ static constexpr int kv_p(int b) { return TF32 ? 2 * KV_QT + b * KV_QT : KV_DP + KV_HALF / 2; }
+  // P^T: tf32 its own buffer; 16-bit packed into the dP^T buffer
+  __host__ __device__ static constexpr int kv_p() { return TF32 ? 2 * KV_QT : KV_DP + KV_HALF / 2; }
   // dQ kernel TMEM map (lanes = queries): S, then a dP buffer (dS after the
   // compute pass: tf32 in place, 16-bit packed per half), then the dQ
   // accumulator.
@@ -230,6 +241,7 @@ struct BwdConfig {
   static constexpr int Q_SMEM = 1024 + 2 * BIG_TILE + Q_KST * Q_KSTAGE_BYTES + Q_VST * Q_VSTAGE_BYTES + NUM_BARS * 8 + 16;
   static constexpr int THREADS = 320;
   static_assert(KV_ST >= 1 && Q_KST >= 1 && Q_VST >= 1, "shared memory budget");
+  static_assert(10 + 2 * KV_PARTS * KV_ST <= NUM_BARS, "dK/dV kernel barriers");
   static_assert(Q_SMEM <= 232448, "dQ kernel shared memory");
   static_assert(KV_DV + HD <= 512 && Q_DQ + HD <= 512, "TMEM budget");
   static_assert(HD * EB % 128 == 0, "head dim must fill whole 128-byte rows");
@@ -431,9 +443,12 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + ST * C::KV_STAGE_BYTES);
   uint64_t* kv_full = bars;
   uint64_t* kv_empty = kv_full + 1;
-  uint64_t* q_full = kv_empty + 1;  // [ST]
-  uint64_t* q_empty = q_full + ST;  // [ST]
-  uint64_t* s_full = q_empty + ST;
+  constexpr int NP = C::KV_PARTS;
+  uint64_t* part_full = kv_empty + 1;          // [NP][ST]
+  uint64_t* part_empty = part_full + NP * ST;  // [NP][ST]
+  auto pfull = [&](int part, int st) { return &part_full[part * ST + st]; };
+  auto pempty = [&](int part, int st) { return &part_empty[part * ST + st]; };
+  uint64_t* s_full = part_empty + NP * ST;
   uint64_t* s_free = s_full + 1;
   uint64_t* dp_full = s_free + 1;
   uint64_t* p_full = dp_full + 1;   // dS^T (and 16-bit P^T) stored
@@ -464,9 +479,9 @@ __global__ void __launch_bounds__(320, 1)
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
     mbar_init(kv_empty, 1);
-    for (int s = 0; s < ST; ++s) {
-      mbar_init(&q_full[s], 1);
-      mbar_init(&q_empty[s], 1);
+    for (int s = 0; s < NP * ST; ++s) {
+      mbar_init(&part_full[s], 1);
+      mbar_init(&part_empty[s], 1);
     }
     mbar_init(s_full, 1);
     mbar_init(s_free, 256);
@@ -497,7 +512,10 @@ __global__ void __launch_bounds__(320, 1)
       tma_prefetch_desc(&tm_v);
       tma_prefetch_desc(&tm_do);
       int g = 0, ni = 0;  // query tiles and non-empty items issued so far
-      int issued_kv = 0, issued = 0;
+      int issued_kv = 0;
+      int issued[NP];  // query tiles whose part q was issued
+#pragma unroll
+      for (int q = 0; q < NP; ++q) issued[q] = 0;
       bool ok = true;
       for (int r = 0; ok; ++r) {
         const int w = snake_item(r, cta, G);
@@ -516,21 +534,30 @@ __global__ void __launch_bounds__(320, 1)
           tma_load_3d(sV + b * 128 * 128, &tm_v, kv_full, b * C::E128, krow, bh);
         }
         issued_kv = ni + 1;
-        for (int it = 0; it < n_it; ++it, ++g) {
+        for (int it = 0; ok && it < n_it; ++it, ++g) {
           const int st = g % ST;
-          if (!(ok = mbar_wait(&q_empty[st], ((g / ST) & 1) ^ 1, abort_flag, limit, 11))) break;
           const int row = p.q_row0 + (qt_first + it) * QT;
-          mbar_arrive_expect_tx(&q_full[st], C::KV_STAGE_BYTES);
+          // parts in the order the GEMMs read them
 #pragma unroll
-          for (int b = 0; b < C::KBLK; ++b) {
-            tma_load_3d(sQ(st) + b * QT * 128, &tm_q, &q_full[st], b * C::E128, row, bh);
-            tma_load_3d(sdO(st) + b * QT * 128, &tm_do, &q_full[st], b * C::E128, row, bh);
-            if constexpr (C::TF32) {
-              tma_load_3d(sQm(st) + b * QT * 128, &tm_qm, &q_full[st], b * C::E128, row, bh);
-              tma_load_3d(sdOm(st) + b * QT * 128, &tm_dom, &q_full[st], b * C::E128, row, bh);
+          for (int q = 0; q < NP; ++q) {
+            if (!(ok = mbar_wait(pempty(q, st), ((g / ST) & 1) ^ 1, abort_flag, limit, 11))) break;
+            uint64_t* bar = pfull(q, st);
+            if constexpr (NP == 1) {
+              mbar_arrive_expect_tx(bar, C::KV_STAGE_BYTES);
+#pragma unroll
+              for (int b = 0; b < C::KBLK; ++b) {
+                tma_load_3d(sQ(st) + b * QT * 128, &tm_q, bar, b * C::E128, row, bh);
+                tma_load_3d(sdO(st) + b * QT * 128, &tm_do, bar, b * C::E128, row, bh);
+              }
+            } else {
+              mbar_arrive_expect_tx(bar, C::KV_QTILE);
+              const CUtensorMap* map = q == 0 ? &tm_q : q == 1 ? &tm_do : q == 2 ? &tm_dom : &tm_qm;
+              uint8_t* dst = q == 0 ? sQ(st) : q == 1 ? sdO(st) : q == 2 ? sdOm(st) : sQm(st);
+#pragma unroll
+              for (int b = 0; b < C::KBLK; ++b) tma_load_3d(dst + b * QT * 128, map, bar, b * C::E128, row, bh);
             }
+            issued[q] = g + 1;
           }
-          issued = g + 1;
         }
         ++ni;
       }
@@ -541,9 +568,11 @@ __global__ void __launch_bounds__(320, 1)
         if (issued_kv > 0)
           while (!mbar_try_wait(kv_full, (issued_kv - 1) & 1) && globaltimer_ns() - t0 < limit) {
           }
-        for (int it = max(0, issued - ST); it < issued; ++it)
-          while (!mbar_try_wait(&q_full[it % ST], (it / ST) & 1) && globaltimer_ns() - t0 < limit) {
-          }
+#pragma unroll
+        for (int q = 0; q < NP; ++q)
+          for (int it = max(0, issued[q] - ST); it < issued[q]; ++it)
+            while (!mbar_try_wait(pfull(q, it % ST), (it / ST) & 1) && globaltimer_ns() - t0 < limit) {
+            }
       }
     }
     __syncwarp();
@@ -580,13 +609,20 @@ __global__ void __launch_bounds__(320, 1)
       if (!(ok = mbar_wait_warp(kv_full, ni & 1, abort_flag, limit, 12))) break;
       // first S^T of the item: the compute warps must have read the last one
       if (g > 0 && !(ok = mbar_wait_warp(s_free, (g - 1) & 1, abort_flag, limit, 14))) break;
-      if (!(ok = mbar_wait_warp(&q_full[g % ST], (g / ST) & 1, abort_flag, limit, 13))) break;
+      if (!(ok = mbar_wait_warp(pfull(0, g % ST), (g / ST) & 1, abort_flag, limit, 13))) break;
       tc_fence_after();
       if (elect_one()) {
         gemm_ss(tbase + C::KV_S, aK, smem_u32(sQ(g % ST)));
         umma_commit(s_full);
+        if constexpr (NP > 1) umma_commit(pempty(0, g % ST));
+      }
+      __syncwarp();
+      if (NP > 1 && !(ok = mbar_wait_warp(pfull(1, g % ST), (g / ST) & 1, abort_flag, limit, 38))) break;
+      tc_fence_after();
+      if (elect_one()) {
         gemm_ss(tbase + C::KV_DP, aV, smem_u32(sdO(g % ST)));
         umma_commit(dp_full);
+        if constexpr (NP > 1) umma_commit(pempty(1, g % ST));
         if (n_it == 1) umma_commit(kv_empty);
       }
       __syncwarp();
@@ -601,11 +637,12 @@ __global__ void __launch_bounds__(320, 1)
         auto issue_next_s = [&](bool wait_s_free) -> bool {
           if (it + 1 < n_it) {
             if (wait_s_free && !mbar_wait_warp(s_free, g & 1, abort_flag, limit, 14)) return false;
-            if (!mbar_wait_warp(&q_full[st1], ((g + 1) / ST) & 1, abort_flag, limit, 15)) return false;
+            if (!mbar_wait_warp(pfull(0, st1), ((g + 1) / ST) & 1, abort_flag, limit, 15)) return false;
             tc_fence_after();
             if (elect_one()) {
               gemm_ss(tbase + C::KV_S, aK, smem_u32(sQ(st1)));
               umma_commit(s_full);
+              if constexpr (NP > 1) umma_commit(pempty(0, st1));
             }
             __syncwarp();
           }
@@ -619,8 +656,12 @@ __global__ void __launch_bounds__(320, 1)
           if (!(ok = mbar_wait_warp(pt_full, g & 1, abort_flag, limit, 37))) break;
           // the accumulators are free once the previous item's epilogue read them
           if (it == 0 && ni > 0 && !(ok = mbar_wait_warp(acc_free, (ni - 1) & 1, abort_flag, limit, 34))) break;
+          if (NP > 1 && !(ok = mbar_wait_warp(pfull(2, st), (g / ST) & 1, abort_flag, limit, 39))) break;
           tc_fence_after();
-          if (elect_one()) gemm_ts(tbase + C::KV_DV, tbase + C::kv_p(g & 1), smem_u32(sdOm(st)), it > 0);
+          if (elect_one()) {
+            gemm_ts(tbase + C::KV_DV, tbase + C::kv_p(), smem_u32(sdOm(st)), it > 0);
+            if constexpr (NP > 1) umma_commit(pempty(2, st));
+          }
           __syncwarp();
           // every compute thread arrives on s_free (S^T read) before pt_full,
           // so the completed pt_full phase implies the s_free one
@@ -629,20 +670,26 @@ __global__ void __launch_bounds__(320, 1)
         if (!(ok = mbar_wait_warp(p_full, g & 1, abort_flag, limit, 16))) break;
         if (!C::EARLY_P && it == 0 && ni > 0 && !(ok = mbar_wait_warp(acc_free, (ni - 1) & 1, abort_flag, limit, 34)))
           break;
+        if (NP > 1 && !(ok = mbar_wait_warp(pfull(NP - 1, st), (g / ST) & 1, abort_flag, limit, 40))) break;
         tc_fence_after();
         if (elect_one()) {
-          if constexpr (!C::EARLY_P) gemm_ts(tbase + C::KV_DV, tbase + C::kv_p(0), smem_u32(sdOm(st)), it > 0);
+          if constexpr (!C::EARLY_P) gemm_ts(tbase + C::KV_DV, tbase + C::kv_p(), smem_u32(sdOm(st)), it > 0);
           gemm_ts(tbase + C::KV_DK, tbase + C::KV_DP, smem_u32(sQm(st)), it > 0);
-          umma_commit(&q_empty[st]);
-          if (it + 1 < n_it) {
-            gemm_ss(tbase + C::KV_DP, aV, smem_u32(sdO(st1)));
-            umma_commit(dp_full);
-            if (it + 2 == n_it) umma_commit(kv_empty);  // last GEMMs reading K / V of this item
-          } else {
-            umma_commit(acc_full);
-          }
+          umma_commit(pempty(NP - 1, st));
+          if (it + 1 == n_it) umma_commit(acc_full);
         }
         __syncwarp();
+        if (it + 1 < n_it) {
+          if (NP > 1 && !(ok = mbar_wait_warp(pfull(1, st1), ((g + 1) / ST) & 1, abort_flag, limit, 41))) break;
+          tc_fence_after();
+          if (elect_one()) {
+            gemm_ss(tbase + C::KV_DP, aV, smem_u32(sdO(st1)));
+            umma_commit(dp_full);
+            if constexpr (NP > 1) umma_commit(pempty(1, st1));
+            if (it + 2 == n_it) umma_commit(kv_empty);  // last GEMMs reading K / V of this item
+          }
+          __syncwarp();
+        }
       }
       ++ni;
     }
@@ -720,9 +767,9 @@ __global__ void __launch_bounds__(320, 1)
             if (c < cmin) sv[c] = 0.f;
         }
         if constexpr (C::EARLY_P) {
-          // P^T (buffer g % 2: dV of tile g-2, its last reader, completed
-          // before S^T of this tile, which the s_full wait above covered)
-          tmem_store_operand<DT>(tbase + lane_off + C::kv_p(g & 1) + h * HALF, sv);
+          // P^T over the previous tile's (its reader, dV of tile g-1, was
+          // queued before S^T of this tile, which the s_full wait above covered)
+          tmem_store_operand<DT>(tbase + lane_off + C::kv_p() + h * HALF, sv);
           tmem_wait_st();
           tc_fence_before();
           mbar_arrive(pt_full);
@@ -754,7 +801,7 @@ __global__ void __launch_bounds__(320, 1)
           else
             tmem_store_operand<DT>(tbase + lane_off + C::KV_DP + h * HALF + ch * 16, dsv);
         }
-        if constexpr (!C::EARLY_P) tmem_store_operand<DT>(tbase + lane_off + C::kv_p(0) + h * HALF, sv);
+        if constexpr (!C::EARLY_P) tmem_store_operand<DT>(tbase + lane_off + C::kv_p() + h * HALF, sv);
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(p_full);
