@@ -219,7 +219,16 @@ struct BwdConfig {
   // A second dP^T buffer (so the next dP^T GEMM is queued before the compute
   // warps release the current one) measured 4-8% slower: thread-side TMEM
   // loads/stores take ~4x longer while the tensor pipe is busy.
-  static constexpr int KV_HALF = KV_QT / 2;  // score columns per compute warpgroup
+  // Compute warpgroups of the dK/dV kernel (thread = key row x KV_HALF query
+  // columns) plus the TMA and MMA warps.  tf32: four (576 threads, 96
+  // registers each), so that each SM sub-partition interleaves four warps'
+  // TMEM load -> exp / dS -> TMEM store chains (0.094 -> 0.089 ms at config
+  // 2; handing the producer warps' registers over with setmaxnreg made their
+  // 56-register loops spill).
+  static constexpr int KV_GROUPS = TF32 ? 4 : 2;
+  static constexpr int KV_HALF = KV_QT / KV_GROUPS;  // score columns per compute warpgroup
+  static constexpr int KV_THREADS = KV_GROUPS * 128 + 64;
+  static_assert(KV_GROUPS == 2 || HD == 64, "four compute groups split the dK|dV epilogue in 32-column quarters");
   static constexpr bool EARLY_P = TF32;
   static constexpr int KV_S = 0;
   static constexpr int KV_DP = KV_QT;
@@ -239,7 +248,7 @@ struct BwdConfig {
   static constexpr int NUM_BARS = 32;
   static constexpr int KV_SMEM = 1024 + 2 * BIG_TILE + KV_ST * KV_STAGE_BYTES + NUM_BARS * 8 + 16;
   static constexpr int Q_SMEM = 1024 + 2 * BIG_TILE + Q_KST * Q_KSTAGE_BYTES + Q_VST * Q_VSTAGE_BYTES + NUM_BARS * 8 + 16;
-  static constexpr int THREADS = 320;
+  static constexpr int THREADS = 320;  // dQ kernel: 8 compute warps, TMA warp, MMA warp
   static_assert(KV_ST >= 1 && Q_KST >= 1 && Q_VST >= 1, "shared memory budget");
   static_assert(10 + 2 * KV_PARTS * KV_ST <= NUM_BARS, "dK/dV kernel barriers");
   static_assert(Q_SMEM <= 232448, "dQ kernel shared memory");
@@ -418,7 +427,7 @@ __device__ __forceinline__ int snake_item(int r, int c, int G) { return r * G + 
 // GEMMs ran; the next item's GEMMs overlap the current epilogue.
 // ---------------------------------------------------------------------------
 template <typename DT, int HD>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(BwdConfig<DT, HD>::KV_THREADS, 1)
     attn_bwd_dkdv_sm100(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                         const __grid_constant__ CUtensorMap tm_qm, const __grid_constant__ CUtensorMap tm_dom,
@@ -429,7 +438,9 @@ __global__ void __launch_bounds__(320, 1)
   constexpr int HALF = C::KV_HALF;
   constexpr int kKind = DTypeTraits<DT>::kKind;
   constexpr uint32_t kFmt = DTypeTraits<DT>::kFmt;
-  constexpr int TMA_WARP = 8, MMA_WARP = 9;
+  constexpr int CW = 4 * C::KV_GROUPS;  // compute warps
+  constexpr int CT = 128 * C::KV_GROUPS;  // compute threads
+  constexpr int TMA_WARP = CW, MMA_WARP = CW + 1;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -484,12 +495,12 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&part_empty[s], 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(s_free, 256);
+    mbar_init(s_free, CT);
     mbar_init(dp_full, 1);
-    mbar_init(p_full, 256);
-    mbar_init(pt_full, 256);
+    mbar_init(p_full, CT);
+    mbar_init(pt_full, CT);
     mbar_init(acc_full, 1);
-    mbar_init(acc_free, 256);
+    mbar_init(acc_free, CT);
     mbar_init(done_bar, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -701,9 +712,9 @@ __global__ void __launch_bounds__(320, 1)
     while (!mbar_try_wait(done_bar, 0) && globaltimer_ns() - t0 < limit) {
     }
     __syncwarp();
-  } else if (warp < 8) {
+  } else if (warp < CW) {
     // --------------------------- compute warps ---------------------------
-    const int h = threadIdx.x >> 7;   // column half
+    const int h = threadIdx.x >> 7;   // column group
     const int rr = threadIdx.x & 127;  // key row inside the tile (TMEM lane)
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const float sl2 = p.scale_log2;
@@ -723,11 +734,19 @@ __global__ void __launch_bounds__(320, 1)
       const size_t row_index = (size_t)bh * p.k_rows_alloc + p.k_row0 + key;
       if (n_it == 0) {  // no query sees this key tile: dK = dV = 0
         if (!p.accumulate && key_ok) {
-          uint32_t zero[HD / 2];
+          if constexpr (C::KV_GROUPS == 4) {
+            uint32_t zero[32];
 #pragma unroll
-          for (int i = 0; i < HD / 2; ++i) zero[i] = 0u;
-          row_store<DT, HD / 2>(zero, reinterpret_cast<DT*>(p.dk) + row_index * HD + col, false);
-          row_store<DT, HD / 2>(zero, reinterpret_cast<DT*>(p.dv) + row_index * HD + col, false);
+            for (int i = 0; i < 32; ++i) zero[i] = 0u;
+            row_store<DT, 32>(zero, reinterpret_cast<DT*>(h < 2 ? p.dk : p.dv) + row_index * HD + (h & 1) * 32,
+                              false);
+          } else {
+            uint32_t zero[HD / 2];
+#pragma unroll
+            for (int i = 0; i < HD / 2; ++i) zero[i] = 0u;
+            row_store<DT, HD / 2>(zero, reinterpret_cast<DT*>(p.dk) + row_index * HD + col, false);
+            row_store<DT, HD / 2>(zero, reinterpret_cast<DT*>(p.dv) + row_index * HD + col, false);
+          }
         }
         continue;
       }
@@ -810,7 +829,16 @@ __global__ void __launch_bounds__(320, 1)
       // ------------------------------ epilogue ------------------------------
       if (!(ok = mbar_wait(acc_full, ni & 1, abort_flag, limit, 19))) break;
       tc_fence_after();
-      if (p.accumulate) {
+      if constexpr (C::KV_GROUPS == 4) {
+        // groups 0, 1: the two 32-column halves of dK; 2, 3: of dV
+        const uint32_t src = tbase + lane_off + (h < 2 ? C::KV_DK : C::KV_DV) + (h & 1) * 32;
+        void* dst_row = reinterpret_cast<char*>(h < 2 ? p.dk : p.dv) +
+                        (row_index * HD + (h & 1) * 32) * (p.accumulate ? sizeof(float) : sizeof(DT));
+        if (p.accumulate)
+          tmem_row_accumulate<32>(src, reinterpret_cast<float*>(dst_row), key_ok);
+        else
+          tmem_row_to_global<DT, 32>(src, reinterpret_cast<DT*>(dst_row), key_ok, false);
+      } else if (p.accumulate) {
         tmem_row_accumulate<HD / 2>(tbase + lane_off + C::KV_DK + col,
                                     reinterpret_cast<float*>(p.dk) + row_index * HD + col, key_ok);
         tmem_row_accumulate<HD / 2>(tbase + lane_off + C::KV_DV + col,

@@ -483,7 +483,7 @@ int launch_bwd_tc(const Problem& pr, const void* q, const void* k, const void* v
   // persistent: one CTA per SM (or per item when there are fewer items)
   const long long kv_items = (long long)n_kt * BH;
   const unsigned kv_grid = (unsigned)std::min<long long>(kv_items, sm_count());
-  kdkdv<<<kv_grid, C::THREADS, C::KV_SMEM, stream>>>(kv_q, kv_k, kv_v, kv_do, kv_qm, kv_dom, p, n_kt, (int)kv_items);
+  kdkdv<<<kv_grid, C::KV_THREADS, C::KV_SMEM, stream>>>(kv_q, kv_k, kv_v, kv_do, kv_qm, kv_dom, p, n_kt, (int)kv_items);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch attn_bwd_dkdv_sm100");
   record(ev, 2, stream);
