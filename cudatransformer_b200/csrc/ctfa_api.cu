@@ -308,7 +308,7 @@ int forward_impl(const Problem& pr, const void* q, const void* k, const void* v,
         void* r[3] = {w, w + align256(n * 4), w + 2 * align256(n * 4)};
         // rounding to tf32 happens inside the kernel, which also writes the
         // rounded copies the backward reads (CTFA_DTYPE_TF32)
-        return pr.D == 64 ? launch_fwd_tc<float, 64, 2, 128, 3, 2, true>(pr, q, k, v, o, lse, stream, r)
+        return pr.D == 64 ? launch_fwd_tc<float, 64, 2, 128, 2, 2, true>(pr, q, k, v, o, lse, stream, r)
                           : launch_fwd_tc<float, 128, 1, 64, 3, 2, true>(pr, q, k, v, o, lse, stream, r);
       }
       case CTFA_DTYPE_TF32:
