@@ -115,10 +115,9 @@ __device__ __forceinline__ void vec_to_float(const uint4& u, float* f) {
 }
 
 template <typename DT, int HD>
-__global__ void __launch_bounds__(256) attn_bwd_prep(BwdPrepParams p) {
+__device__ __forceinline__ void attn_bwd_prep_rowgroup(const BwdPrepParams& p, long long t) {
   using S = PrepShape<DT, HD>;
   constexpr int VEC = S::VEC, TPR = S::TPR, VPT = S::VPT;
-  const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const long long w = t / TPR;  // padded query row
   const int sub = (int)(t % TPR);
   // whole row groups share a warp; every lane reaches the shuffles below
@@ -164,6 +163,19 @@ __global__ void __launch_bounds__(256) attn_bwd_prep(BwdPrepParams p) {
       p.lse2[w] = INFINITY;
     }
   }
+}
+
+// Grid-stride over row groups with one resident wave of blocks (a grid of
+// rows * TPR / 256 blocks left the last wave ~30 % full at config 2); the
+// loop advances whole warps, so every lane reaches the shuffles below.
+template <typename DT, int HD>
+__global__ void __launch_bounds__(256) attn_bwd_prep(BwdPrepParams p) {
+  using S = PrepShape<DT, HD>;
+  constexpr int VEC = S::VEC, TPR = S::TPR, VPT = S::VPT;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  const long long total = p.rows * TPR;
+  for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t - (threadIdx.x & 31) < total; t += stride)
+    attn_bwd_prep_rowgroup<DT, HD>(p, t);
 }
 
 template <typename DT, int HD>

@@ -429,7 +429,9 @@ int launch_bwd_tc(const Problem& pr, const void* q, const void* k, const void* v
   pp.delta = delta;
   pp.dO_round = (dO_mma != dO) ? reinterpret_cast<float*>(const_cast<void*>(dO_mma)) : nullptr;
   if (!std::is_same<DT, float>::value) record(ev, 0, stream);
-  attn_bwd_prep<DT, HD><<<(unsigned)((pp.rows * PrepShape<DT, HD>::TPR + 255) / 256), 256, 0, stream>>>(pp);
+  const long long prep_blocks =
+      std::max<long long>(1, std::min<long long>((pp.rows * PrepShape<DT, HD>::TPR + 255) / 256, sm_count() * 8));
+  attn_bwd_prep<DT, HD><<<(unsigned)prep_blocks, 256, 0, stream>>>(pp);
   record(ev, 1, stream);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch attn_bwd_prep");
