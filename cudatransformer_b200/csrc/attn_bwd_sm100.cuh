@@ -9,7 +9,7 @@
 //
 //   attn_bwd_prep     delta_i = sum_d O_i[d] dO_i[d]            (HBM-bound)
 //   attn_bwd_dkdv     per key tile (128 keys, stationary K, V); streams
-//                     query tiles (Q, dO) through ST stages:
+//                     128-query tiles (Q, dO) through ST stages:
 //                       S^T  = K Q^T        (SS)   -> TMEM
 //                       dP^T = V dO^T       (SS)   -> TMEM
 //                       P^T  = exp2(S^T*scale*log2e - lse_q*log2e), masked
@@ -23,11 +23,15 @@
 // dQ is produced by its own query-stationary pass instead of atomics, so all
 // three gradients are written once, deterministically, in the I/O type.
 //
-// Warp roles in both main kernels: warps 0..7 = two compute warpgroups that
-// split the 128 score columns (64 each; thread = TMEM lane = row), warp 8 =
-// TMA producer, warp 9 = MMA issuer.  The score buffer S is released as soon
-// as the compute warps have it in registers, so the next S GEMM overlaps the
-// exponentials of the current tile.
+// Warp roles in both main kernels: compute warpgroups that split the 128
+// score columns (thread = TMEM lane = row; dQ and 16-bit dK/dV: two groups
+// of 64 columns, tf32 dK/dV: four of 32), then the TMA producer warp and the
+// MMA-issuing warp.  The score buffer S is released as soon as the compute
+// warps have it in registers, so the next S GEMM overlaps the exponentials of
+// the current tile.  The tensor pipe takes a thread's next MMA only as it
+// starts the previous one, so the MMA warp's issue order is chosen to keep
+// it from waiting while a GEMM is ready (dK/dV: dV_g, S^T_{g+1}, dK_g,
+// dP^T_{g+1}).
 #pragma once
 
 #include "sm100_primitives.cuh"
