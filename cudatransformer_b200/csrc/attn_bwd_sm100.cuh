@@ -174,8 +174,7 @@ __device__ __forceinline__ void attn_bwd_prep_rowgroup(const BwdPrepParams& p, l
 // loop advances whole warps, so every lane reaches the shuffles below.
 template <typename DT, int HD>
 __global__ void __launch_bounds__(256) attn_bwd_prep(BwdPrepParams p) {
-  using S = PrepShape<DT, HD>;
-  constexpr int VEC = S::VEC, TPR = S::TPR, VPT = S::VPT;
+  constexpr int TPR = PrepShape<DT, HD>::TPR;
   const long long stride = (long long)gridDim.x * blockDim.x;
   const long long total = p.rows * TPR;
   for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t - (threadIdx.x & 31) < total; t += stride)
