@@ -17,10 +17,11 @@
 //   warp  4*NQ+1    : tcgen05.mma issuer (one elected lane).
 //   warps 4*NQ+2,3  : complete the producer warpgroup, which hands its
 //                     registers to the softmax warpgroups via setmaxnreg.  For
-//                     fp32 I/O (RND) they round every landed Q/K/V tile to tf32
+//                     fp32 I/O (RND) they round every landed K/V tile to tf32
 //                     (round to nearest) in shared memory before the MMAs read
-//                     it, and store the rounded tiles for the backward: Q by
-//                     every CTA, each K/V tile by one designated CTA.
+//                     it and store it for the backward (each K/V tile by one
+//                     designated CTA); the softmax warpgroups do the same for
+//                     their Q tiles before the first S tile (Q by every CTA).
 //
 //   V is the MN-major B operand of P V: 128B swizzle for 16-bit types, the
 //   32-byte-granule variant for tf32.
@@ -182,7 +183,7 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
       mbar_init(&v_empty[s], RND ? 2 : 1);
       mbar_init(&v_ready[s], 64);
     }
-    mbar_init(q_ready, 64);
+    mbar_init(q_ready, NQ * 128);  // RND: the softmax warpgroups round Q
     for (int k = 0; k < NQ; ++k) {
       mbar_init(&s_full[k], 1);
       mbar_init(&p_full[k], 128);
@@ -378,24 +379,9 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
     // K/V tile t of this head is stored by the one CTA whose query group
     // contains key row t*BN (it loads the tile under the causal mask too).
     auto designated = [&](int t) { return min((t * BN) / (NQ * BM), p.n_groups - 1) == group; };
+    // (the Q tiles are rounded and stored by the softmax warpgroups, which
+    // are idle until the first S tile)
     bool ok = n_max > 0;
-    if (ok && (ok = mbar_wait(q_full, 0, abort_flag, limit, 42))) {
-#pragma unroll
-      for (int k = 0; k < NQ; ++k)
-        if (n_kv[k] > 0) round_tile(sQ + k * C::Q_TILE_BYTES, C::Q_TILE_BYTES);
-      mbar_arrive(q_ready);
-      if (leader && (ok = mbar_wait(q_ready, 0, abort_flag, limit, 45))) {
-#pragma unroll
-        for (int k = 0; k < NQ; ++k) {
-          if (n_kv[k] == 0) continue;
-          const int row = p.q_row0 + (group * NQ + k) * BM;
-#pragma unroll
-          for (int b = 0; b < C::KBLK; ++b)
-            tma_store_3d(&tm_qr, sQ + k * C::Q_TILE_BYTES + b * BM * 128, b * C::E128, row, bh);
-        }
-        tma_store_commit();
-      }
-    }
     for (int t = 0; ok && t < n_max; ++t) {
       const bool mine = designated(t);
       const int kst = t % KST, vst = t % VST;
@@ -441,6 +427,44 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
     const uint32_t s_addr = tbase + lane_off + k * BN;
     const uint32_t o_addr = tbase + lane_off + NQ * BN + k * HD;
     const float sl2 = p.scale_log2;
+    bool q_stored = false;
+    if constexpr (RND) {
+      // Round this warpgroup's Q tile in place (four 16-byte loads in flight
+      // per thread), then its thread 0 stores the rounded tile for the
+      // backward.  The whole warpgroup takes the named barrier whatever the
+      // wait returned, so that no thread is left waiting on it.
+      const bool qok = mbar_wait(q_full, 0, abort_flag, limit, 42);
+      if (qok && n > 0) {
+        float4* t4 = reinterpret_cast<float4*>(sQ + k * C::Q_TILE_BYTES);
+        static_assert(C::Q_TILE_BYTES % (16 * 4 * 128) == 0, "Q rounding split");
+        for (int i = r; i < C::Q_TILE_BYTES / 16; i += 4 * 128) {
+          float4 x[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) x[u] = t4[i + u * 128];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            x[u].x = __uint_as_float(f32_to_tf32_rna(x[u].x));
+            x[u].y = __uint_as_float(f32_to_tf32_rna(x[u].y));
+            x[u].z = __uint_as_float(f32_to_tf32_rna(x[u].z));
+            x[u].w = __uint_as_float(f32_to_tf32_rna(x[u].w));
+            t4[i + u * 128] = x[u];
+          }
+        }
+        fence_proxy_async_smem();
+      }
+      mbar_arrive(q_ready);
+      if (n > 0) {
+        named_bar_sync(1 + k, 128);
+        if (r == 0 && qok) {
+          const int row = p.q_row0 + qt * BM;
+#pragma unroll
+          for (int b = 0; b < C::KBLK; ++b)
+            tma_store_3d(&tm_qr, sQ + k * C::Q_TILE_BYTES + b * BM * 128, b * C::E128, row, bh);
+          tma_store_commit();
+          q_stored = true;
+        }
+      }
+    }
     float m = -INFINITY;
     float l = 0.f;
     bool ok = true;
@@ -585,6 +609,7 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
         p.lse[row_index] = l > 0.f ? (m_use + __log2f(l)) * 0.69314718055994531f : -INFINITY;
       }
     }
+    if (q_stored) tma_store_wait_all();
   }
 
   tc_fence_before();
