@@ -431,9 +431,11 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
     if constexpr (RND) {
       // Round this warpgroup's Q tile in place (four 16-byte loads in flight
       // per thread), then its thread 0 stores the rounded tile for the
-      // backward.  The whole warpgroup takes the named barrier whatever the
-      // wait returned, so that no thread is left waiting on it.
-      const bool qok = mbar_wait(q_full, 0, abort_flag, limit, 42);
+      // backward.  Only tiles with keys to attend to were loaded (a CTA with
+      // none loads no Q at all), so only their warpgroups wait for Q; the
+      // whole warpgroup takes the named barrier whatever the wait returned,
+      // so that no thread is left waiting on it.
+      const bool qok = n > 0 && mbar_wait(q_full, 0, abort_flag, limit, 42);
       if (qok && n > 0) {
         float4* t4 = reinterpret_cast<float4*>(sQ + k * C::Q_TILE_BYTES);
         static_assert(C::Q_TILE_BYTES % (16 * 4 * 128) == 0, "Q rounding split");
