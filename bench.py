@@ -577,7 +577,8 @@ def run_ours(args, w):
                 "copies_only_ms_per_step": round(ms_copies / args.steps, 4),
                 "of_copy_floor": round(ms_copies / ms_e2e, 3),
                 "copy_floor_gbs_per_direction": round(4 * nbytes / (ms_copies / args.steps * 1e-3) / 1e9, 1)},
-        "gpu_launches": (5 if fws_bytes else 4) * args.steps,
+        # per step: forward (tf32 rounding inside it), delta pass, dK/dV, dQ
+        "gpu_launches": 4 * args.steps,
         "roofline": {"kernel": dom, "bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1),
                      "unit": "TFLOP/s", "frac": round(achieved / peak, 3) if peak else None,
                      "peak_source": peak_note, "flops_per_launch": kflops[dom],
