@@ -319,7 +319,7 @@ int forward_impl(const Problem& pr, const void* q, const void* k, const void* v,
                           : launch_fwd_tc<__nv_bfloat16, 128, 2, 128, 2, 2>(pr, q, k, v, o, lse, stream);
       default:
         return pr.D == 64 ? launch_fwd_tc<__half, 64, 2, 128, 4, 3>(pr, q, k, v, o, lse, stream)
-                          : launch_fwd_tc<__half, 128, 2, 128, 3, 2>(pr, q, k, v, o, lse, stream);
+                          : launch_fwd_tc<__half, 128, 2, 128, 2, 2>(pr, q, k, v, o, lse, stream);
     }
   }
   switch (pr.dtype) {
