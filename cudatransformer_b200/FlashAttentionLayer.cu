@@ -27,6 +27,13 @@
 //     backward.  cachedMaxScores holds the same logsumexp in DType and
 //     cachedDenominators holds ones, so exp(s - max) / denom is still the
 //     softmax for code that reads the old fields.
+//   * float: the forward writes round-to-nearest tf32 copies of q, k, v into
+//     its workspace (include/ctfa.h).  With saveStates that workspace is kept
+//     with the other cached state, and computeBackward on the same q, k, v
+//     buffers passes the copies to the backward (CTFA_DTYPE_TF32), which then
+//     rounds only dO.  Like the reference's cached output and max/denominator
+//     (FlashAttentionLayer.cu:81-84, :114-127), the cache assumes q, k, v were
+//     not modified in place between the two calls.
 // Errors: every non-zero status from the library throws std::runtime_error
 // (the reference throws from cudaMakeShared and ignores launch errors).
 #include "ModuleLayer.cu"
@@ -49,6 +56,10 @@ struct FlashAttentionLayer {
 
   bool causal = false;                        /// key j visible to query i iff j <= i
   std::shared_ptr<float[]> cachedLSE = nullptr;  /// fp32 logsumexp per row
+  /// float only: the forward workspace holding tf32-rounded q, k, v, and the
+  /// buffers they were rounded from
+  std::shared_ptr<unsigned char[]> cachedRounded = nullptr;
+  const void* cachedRoundedFrom[3] = {nullptr, nullptr, nullptr};
 
   FlashAttentionLayer(int headDim, int numHeads, bool causal = false)
       : headDim(headDim), numHeads(numHeads), causal(causal) {}
@@ -68,8 +79,13 @@ struct FlashAttentionLayer {
     const size_t rows = (size_t)batchSize * numHeads * sequenceLength;
     Tensor<DType> output = ctfa_dropin::stream_tensor<DType>(queries.shape().toVector());
     std::shared_ptr<float[]> lse = ctfa_dropin::stream_buffer<float>(rows);
-    runForward(queries, keys, values, output.data(), lse.get(), batchSize, sequenceLength);
+    std::shared_ptr<unsigned char[]> ws =
+        runForward(queries, keys, values, output.data(), lse.get(), batchSize, sequenceLength);
     if (saveStates) {
+      cachedRounded = ws;
+      cachedRoundedFrom[0] = queries.get();
+      cachedRoundedFrom[1] = keys.get();
+      cachedRoundedFrom[2] = values.get();
       cachedLSE = lse;
       cachedMaxScores = ctfa_dropin::stream_buffer<DType>(rows);
       castKernel<float, DType><<<(rows + 255) / 256, 256>>>(lse.get(), cachedMaxScores.get(), rows);
@@ -105,13 +121,21 @@ struct FlashAttentionLayer {
       lse = ctfa_dropin::stream_buffer<float>(rows);
       runForward(queries, keys, values, output.get(), lse.get(), batchSize, sequenceLength);
     }
-    const int code = ctfa_dropin::DtypeCode<DType>::value;
+    int code = ctfa_dropin::DtypeCode<DType>::value;
+    const void* in[3] = {queries.get(), keys.get(), values.get()};
+    if (cachedRounded != nullptr && output == cachedOutput && in[0] == cachedRoundedFrom[0] &&
+        in[1] == cachedRoundedFrom[1] && in[2] == cachedRoundedFrom[2]) {
+      // the forward's tf32-rounded copies of these very buffers, at byte
+      // offsets 0, a, 2a of its workspace (a = B*H*T*D*4 rounded up to 256)
+      const size_t a = (rows * headDim * sizeof(float) + 255) / 256 * 256;
+      for (int i = 0; i < 3; ++i) in[i] = cachedRounded.get() + i * a;
+      code = CTFA_DTYPE_TF32;
+    }
     const size_t wsBytes = ctfa_backward_workspace_bytes(batchSize, numHeads, sequenceLength, headDim, code);
     std::shared_ptr<unsigned char[]> ws = ctfa_dropin::stream_buffer<unsigned char>(wsBytes > 0 ? wsBytes : 256);
-    ctfa_dropin::check(ctfa_backward(queries.get(), keys.get(), values.get(), output.get(), outputGrad.get(),
-                                     lse.get(), grads[0].data(), grads[1].data(), grads[2].data(), ws.get(),
-                                     wsBytes, batchSize, numHeads, sequenceLength, headDim, code, causal ? 1 : 0,
-                                     nullptr),
+    ctfa_dropin::check(ctfa_backward(in[0], in[1], in[2], output.get(), outputGrad.get(), lse.get(),
+                                     grads[0].data(), grads[1].data(), grads[2].data(), ws.get(), wsBytes,
+                                     batchSize, numHeads, sequenceLength, headDim, code, causal ? 1 : 0, nullptr),
                        "ctfa_backward");
     return grads;
   }
@@ -122,17 +146,23 @@ struct FlashAttentionLayer {
     cachedDenominators = nullptr;
     cachedOutput = nullptr;
     cachedLSE = nullptr;
+    cachedRounded = nullptr;
+    cachedRoundedFrom[0] = cachedRoundedFrom[1] = cachedRoundedFrom[2] = nullptr;
   }
 
  private:
-  void runForward(const Tensor<DType>& queries, const Tensor<DType>& keys, const Tensor<DType>& values,
-                  DType* output, float* lse, int batchSize, int sequenceLength) {
+  // Runs the forward; returns its workspace (float: the rounded q, k, v;
+  // null when the dtype needs none).
+  std::shared_ptr<unsigned char[]> runForward(const Tensor<DType>& queries, const Tensor<DType>& keys,
+                                              const Tensor<DType>& values, DType* output, float* lse,
+                                              int batchSize, int sequenceLength) {
     const int code = ctfa_dropin::DtypeCode<DType>::value;
     const size_t wsBytes = ctfa_forward_workspace_bytes(batchSize, numHeads, sequenceLength, headDim, code);
     std::shared_ptr<unsigned char[]> ws = ctfa_dropin::stream_buffer<unsigned char>(wsBytes);
     ctfa_dropin::check(ctfa_forward(queries.get(), keys.get(), values.get(), output, lse, batchSize, numHeads,
                                     sequenceLength, headDim, code, causal ? 1 : 0, ws.get(), wsBytes, nullptr),
                        "ctfa_forward");
+    return ws;
   }
 };
 

@@ -661,21 +661,47 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[CTFA_NOALLOC_SC
 constexpr int kMaxDevices = 128;
 std::mutex g_noalloc_mu;
 void* g_noalloc_addr[kMaxDevices] = {};
+CUcontext g_noalloc_ctx[kMaxDevices] = {};
+
+// The driver's cuCtxGetCurrent, fetched through the runtime (no -lcuda).
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+CtxGetCurrentFn ctx_get_current_fn() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(ptr);
+  });
+  return fn;
+}
 
 // Device address of g_noalloc_scratch on the current device.  In host code
 // the array's name is only a host-side stand-in, so the address is looked up
-// once per device (with that device current) and cached.
+// (with that device current) once per device and context and cached.  The
+// cache is keyed on the current context as well as the device: after a
+// cudaDeviceReset the primary context is a new one, the module is loaded
+// again and the array has a new address, which the next call looks up.
 int noalloc_scratch(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (dev < 0 || dev >= kMaxDevices) return fail(CTFA_ERR_UNSUPPORTED, "device index out of range");
+  auto get_ctx = ctx_get_current_fn();
+  if (get_ctx == nullptr) return fail(CTFA_ERR_CUDA, "cuCtxGetCurrent entry point unavailable");
+  CUcontext ctx = nullptr;
+  if (get_ctx(&ctx) != CUDA_SUCCESS) ctx = nullptr;  // none current yet: look the address up below
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_addr[dev] == nullptr) {
+  if (ctx == nullptr || g_noalloc_addr[dev] == nullptr || g_noalloc_ctx[dev] != ctx) {
+    // (the lookup makes the device's primary context current if none is)
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+    if (get_ctx(&ctx) != CUDA_SUCCESS || ctx == nullptr) return fail(CTFA_ERR_CUDA, "no current CUDA context");
     g_noalloc_addr[dev] = p;
+    g_noalloc_ctx[dev] = ctx;
   }
   *out = g_noalloc_addr[dev];
   return CTFA_OK;

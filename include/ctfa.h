@@ -122,7 +122,10 @@ int ctfa_backward_with_events(const void* q, const void* k, const void* v, const
  * CTFA_ERR_WORKSPACE before anything is launched.
  *   - The first call on a device looks up the array's device address
  *     (cudaGetSymbolAddress, with that device current); make that first call
- *     before any stream capture on the device.
+ *     before any stream capture on the device.  The address is cached per
+ *     device and CUDA context: after a cudaDeviceReset the device's next
+ *     context gets a new copy of the array, and the first call made in it
+ *     looks the address up again (so, again, before any capture).
  *   - All calls share the one array and leave their contents in it; calls
  *     that overlap on the GPU (two streams, two host threads) race and must
  *     be serialised by the caller.  Nothing in the array needs to start at zero.

@@ -8,9 +8,10 @@
 // runs the reference's AttentionLayer<float>::forward through it, another
 // its TransformerBlockLayer<float> forward + backward (whose backward stops
 // at the reference AttentionLayer's released attention output, which the
-// output-projection drop-in rejects).  It proves the drop-ins compile where
-// the reference's layers did, and lets a GPU test compare the composed layer
-// with an fp64 restatement.
+// output-projection drop-in rejects), and one that times the
+// FlashAttentionLayer<float> drop-in's forward + backward step.  It proves the
+// drop-ins compile where the reference's layers did, and lets a GPU test
+// compare the composed layer with an fp64 restatement.
 #include "FlashAttentionLayer.cu"  // ours: same include guard as the reference file
 #include "OutputProjectionLayer.cu"  // ours, likewise
 #include "QKVProjectionLayer.cu"  // ours, likewise
@@ -90,6 +91,53 @@ extern "C" int dropin_attention_forward_device(const float* x, const float* wq, 
     Tensor<float> out = layer.forward(view(x, {(size_t)B, (size_t)N, (size_t)E}));
     cudaMemcpyAsync(y, out.data(), out.size() * sizeof(float), cudaMemcpyDeviceToDevice, 0);
     return (int)cudaGetLastError();
+  } catch (const std::exception& e) {
+    g_last_error = e.what();
+    return -1;
+  }
+}
+
+// FlashAttentionLayer<float> (the drop-in) on device-resident [B, H, T, D]
+// buffers: `iters` steps of computeAttention(saveStates=true) +
+// computeBackward + clearCache on the default stream, the way the reference's
+// AttentionLayer drives it (AttentionLayer.cu:87, :141).  Writes the last
+// step's o, dq, dk, dv and the mean step time (CUDA events on the default
+// stream, after one untimed step).
+extern "C" int dropin_flash_step_f32(const float* q, const float* k, const float* v, const float* dO, float* o,
+                                     float* dq, float* dk, float* dv, int B, int H, int T, int D, int causal,
+                                     int iters, float* ms_per_step) {
+  try {
+    FlashAttentionLayer<float> layer(D, H, causal != 0);
+    const std::vector<size_t> shape = {(size_t)B, (size_t)H, (size_t)T, (size_t)D};
+    auto view = [&](const float* p) {
+      return Tensor<float>(std::shared_ptr<float[]>(const_cast<float*>(p), [](float*) {}), shape);
+    };
+    Tensor<float> tq = view(q), tk = view(k), tv = view(v), tdo = view(dO);
+    const size_t n = (size_t)B * H * T * D;
+    auto step = [&](bool keep) {
+      Tensor<float> out = layer.computeAttention(tq, tk, tv, true);
+      std::array<Tensor<float>, 3> g = layer.computeBackward(tq, tk, tv, tdo);
+      layer.clearCache();
+      if (keep) {
+        cudaMemcpyAsync(o, out.data(), n * sizeof(float), cudaMemcpyDeviceToDevice, 0);
+        float* dst[3] = {dq, dk, dv};
+        for (int i = 0; i < 3; ++i) cudaMemcpyAsync(dst[i], g[i].data(), n * sizeof(float), cudaMemcpyDeviceToDevice, 0);
+      }
+    };
+    step(true);
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cudaEventRecord(e0, 0);
+    for (int i = 0; i < iters; ++i) step(false);
+    cudaEventRecord(e1, 0);
+    cudaEventSynchronize(e1);
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    *ms_per_step = iters > 0 ? ms / iters : 0.f;
+    return (int)cudaDeviceSynchronize();
   } catch (const std::exception& e) {
     g_last_error = e.what();
     return -1;

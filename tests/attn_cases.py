@@ -65,3 +65,57 @@ def errors(ours: dict, ref: dict) -> dict:
             x = np.asarray(ours[name], dtype=np.float64)
             out[name] = float(np.abs(x - r).max() / max(np.abs(r).max(), DEN_FLOOR))
     return out
+
+
+def attention_f64_device(q, k, v, do, causal: bool, chunk: int = 16):
+    """Exact float64 attention forward and backward on the GPU (torch fp64
+    matmuls, `chunk` (batch, head) problems at a time): the same math as
+    oracle.attention_f64 / attention_backward_f64 (softmax(q k^T / sqrt(D)),
+    dS = P (dP - rowsum(O dO)), dq = dS k / sqrt(D), dk = dS^T q / sqrt(D),
+    dv = P^T dO), for full-size checks the CPU oracle would take minutes on.
+    q, k, v, do: device tensors [B, H, T, D] already rounded to the I/O type.
+    Returns float64 device tensors o, lse, dq, dk, dv."""
+    B, H, T, D = q.shape
+    f = lambda t: t.reshape(B * H, T, D).to(torch.float64)
+    qq, kk, vv, dd = f(q), f(k), f(v), f(do)
+    outs = {n: torch.empty((B * H, T, D), dtype=torch.float64, device=q.device) for n in ("o", "dq", "dk", "dv")}
+    lse = torch.empty((B * H, T), dtype=torch.float64, device=q.device)
+    scale = 1.0 / np.sqrt(D)
+    mask = torch.triu(torch.ones(T, T, dtype=torch.bool, device=q.device), diagonal=1) if causal else None
+    for a in range(0, B * H, chunk):
+        sl = slice(a, min(a + chunk, B * H))
+        s = torch.matmul(qq[sl], kk[sl].transpose(1, 2)) * scale
+        if mask is not None:
+            s.masked_fill_(mask, float("-inf"))
+        m = s.amax(dim=-1, keepdim=True)
+        p = torch.exp(s - m)
+        l = p.sum(dim=-1, keepdim=True)
+        p /= l
+        del s
+        o = torch.matmul(p, vv[sl])
+        lse[sl] = (m + torch.log(l))[..., 0]
+        outs["o"][sl] = o
+        outs["dv"][sl] = torch.matmul(p.transpose(1, 2), dd[sl])
+        dp = torch.matmul(dd[sl], vv[sl].transpose(1, 2))
+        delta = (o * dd[sl]).sum(dim=-1, keepdim=True)
+        ds = p * (dp - delta)
+        del dp, p
+        outs["dq"][sl] = torch.matmul(ds, kk[sl]) * scale
+        outs["dk"][sl] = torch.matmul(ds.transpose(1, 2), qq[sl]) * scale
+        del ds
+    res = {n: t.reshape(B, H, T, D) for n, t in outs.items()}
+    res["lse"] = lse.reshape(B, H, T)
+    return res
+
+
+def per_head_errors(ours: dict, ref: dict) -> dict:
+    """max|x - x64| / max|x64| for every (batch, head) slice and output, on the
+    device; returns {name: float64 tensor [B, H]}."""
+    out = {}
+    for name in ("o", "dq", "dk", "dv"):
+        x = ours[name].to(torch.float64)
+        r = ref[name]
+        num = (x - r).abs().amax(dim=(-2, -1))
+        den = r.abs().amax(dim=(-2, -1)).clamp_min(DEN_FLOOR)
+        out[name] = num / den
+    return out

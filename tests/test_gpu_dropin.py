@@ -230,3 +230,66 @@ def test_reference_attention_layer_backward_stops_at_released_output(cuda_device
     rc, msg, *_ = _run_block(LIB, params, x, dy, 4, 256, True)
     assert rc == -1
     assert "OutputProjectionLayer" in msg, msg
+
+
+@needs_lib
+def test_flash_dropin_step_config2(cuda_device):
+    """The C++ FlashAttentionLayer<float> drop-in at BASELINE config 2 (B=8
+    H=12 T=1024 D=64, causal), driven the way the reference's AttentionLayer
+    drives it (computeAttention with saveStates, computeBackward, clearCache):
+    its backward reuses the forward's tf32-rounded q, k, v, so its gradients
+    are bitwise those of the Python mirror (which does the same), and its step
+    costs little more than the bare C-ABI calls (the drop-in adds the
+    reference's cached copy of o and stream-ordered allocations)."""
+    import torch
+
+    from cudatransformer_b200 import FlashAttentionLayer, _lib
+
+    lib = ctypes.CDLL(str(LIB))
+    V, I = ctypes.c_void_p, ctypes.c_int
+    lib.dropin_flash_step_f32.argtypes = [V] * 8 + [I] * 6 + [ctypes.POINTER(ctypes.c_float)]
+    lib.dropin_flash_step_f32.restype = I
+    B, H, T, D = 8, 12, 1024, 64
+    g = torch.Generator(device=cuda_device).manual_seed(21)
+    q, k, v = (torch.randn(B, H, T, D, device=cuda_device, generator=g) * 0.5 for _ in range(3))
+    do = torch.randn(B, H, T, D, device=cuda_device, generator=g)
+    outs = [torch.empty_like(q) for _ in range(4)]
+    ms = ctypes.c_float(0.0)
+    rc = lib.dropin_flash_step_f32(*(t.data_ptr() for t in (q, k, v, do, *outs)), B, H, T, D, 1, 20,
+                                   ctypes.byref(ms))
+    assert rc == 0
+    layer = FlashAttentionLayer(D, H, causal=True)
+    o = layer.computeAttention(q, k, v, saveStates=True)
+    grads = layer.computeBackward(q, k, v, do)
+    torch.cuda.synchronize()
+    for name, a, b in zip(("o", "dq", "dk", "dv"), outs, [o, *grads]):
+        assert torch.equal(a, b), name
+
+    # the bare C-ABI step (forward, backward on the forward's rounded copies)
+    code = _lib.CTFA_DTYPE_F32
+    clib = _lib.load()
+    lse = torch.empty(B, H, T, device=cuda_device)
+    fws = torch.empty(clib.ctfa_forward_workspace_bytes(B, H, T, D, code), dtype=torch.uint8, device=cuda_device)
+    qb, kb, vb = _lib.rounded_copies(fws, B, H, T, D)
+    bws = torch.empty(clib.ctfa_backward_workspace_bytes(B, H, T, D, _lib.CTFA_DTYPE_TF32), dtype=torch.uint8,
+                      device=cuda_device)
+    st = torch.cuda.current_stream().cuda_stream
+    x = [torch.empty_like(q) for _ in range(4)]
+
+    def bare():
+        _lib.check(clib.ctfa_forward(q.data_ptr(), k.data_ptr(), v.data_ptr(), x[0].data_ptr(), lse.data_ptr(),
+                                     B, H, T, D, code, 1, fws.data_ptr(), fws.numel(), st), "fwd")
+        _lib.check(clib.ctfa_backward(qb, kb, vb, x[0].data_ptr(), do.data_ptr(), lse.data_ptr(), x[1].data_ptr(),
+                                      x[2].data_ptr(), x[3].data_ptr(), bws.data_ptr(), bws.numel(), B, H, T, D,
+                                      _lib.CTFA_DTYPE_TF32, 1, st), "bwd")
+
+    bare()
+    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s_ev.record()
+    for _ in range(20):
+        bare()
+    e_ev.record()
+    torch.cuda.synchronize()
+    bare_ms = s_ev.elapsed_time(e_ev) / 20
+    print(f"config-2 step: drop-in {ms.value:.4f} ms, bare C ABI {bare_ms:.4f} ms, ratio {ms.value / bare_ms:.3f}")
+    assert ms.value < 1.10 * bare_ms, (ms.value, bare_ms)
