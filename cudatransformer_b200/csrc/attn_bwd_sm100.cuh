@@ -13,12 +13,16 @@
 //                       S^T  = K Q^T        (SS)   -> TMEM
 //                       dP^T = V dO^T       (SS)   -> TMEM
 //                       P^T  = exp2(S^T*scale*log2e - lse_q*log2e), masked
-//                       dS^T = P^T (dP^T - delta_q) * scale
+//                       dS^T = P^T (dP^T - delta_q)   (16-bit: the softmax
+//                              scale is applied once, to dK in the epilogue;
+//                              tf32: dS^T carries it)
 //                       dV  += P^T dO       (TS, P^T from TMEM)
 //                       dK  += dS^T Q       (TS, dS^T from TMEM)
 //   attn_bwd_dq       per query tile (stationary Q, dO); streams K/V tiles:
-//                       S  = Q K^T, dP = dO V^T (SS), dS as above (row-wise
-//                       lse/delta), dQ += dS K (TS, dS from TMEM)
+//                       S  = Q K^T, dP = dO V^T (SS), dS = P (dP - delta)
+//                       (row-wise lse/delta; packed fp32x2 math), dQ += dS K
+//                       (TS, dS from TMEM), the softmax scale applied to dQ
+//                       in the epilogue
 //
 // dQ is produced by its own query-stationary pass instead of atomics, so all
 // three gradients are written once, deterministically, in the I/O type.
@@ -46,22 +50,24 @@ struct BwdPrepParams {
   const void* o;
   const void* dO;
   const float* lse;  // [BH][q_rows_alloc] natural log
-  float* delta;      // [BH][Tq_pad]; 0 on padding rows
-  float* lse2;       // [BH][Tq_pad] lse * log2(e); +inf on padding rows (their P is 0)
+  float* ndelta;     // [BH][Tq_pad] -delta; 0 on padding rows
+  float* nlse2;      // [BH][Tq_pad] -lse * log2(e); -inf on padding rows (their P is 0)
   float* dO_round;   // fp32 I/O only: round-to-nearest tf32 copy of dO (nullable)
 };
 
 struct BwdParams {
   int BH;
   int Tq, Tk;
-  int Tq_pad;        // row stride of lse2 / delta
+  int Tq_pad;        // row stride of nlse2 / ndelta
   int q_row0, k_row0;
   int q_rows_alloc, k_rows_alloc;
   int causal, causal_offset;
   float scale;       // 1/sqrt(D)
   float scale_log2;  // log2(e)/sqrt(D)
-  const float* lse2;   // [BH][Tq_pad] lse * log2(e), +inf on padding rows
-  const float* delta;  // [BH][Tq_pad], 0 on padding rows
+  // Both negated, so that the compute warps form P and dS with packed adds /
+  // FMAs: P = exp2(S * scale*log2e + nlse2), dS = P (dP + ndelta).
+  const float* nlse2;   // [BH][Tq_pad] -lse * log2(e), -inf on padding rows
+  const float* ndelta;  // [BH][Tq_pad] -delta, 0 on padding rows
   void* dq;          // [BH][q_rows_alloc][HD]
   void* dk;          // [BH][k_rows_alloc][HD]
   void* dv;
@@ -160,11 +166,11 @@ __device__ __forceinline__ void attn_bwd_prep_rowgroup(const BwdPrepParams& p, l
   for (int off = TPR / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
   if (in && sub == 0) {
     if (real) {
-      p.delta[w] = s;
-      p.lse2[w] = p.lse[bh * p.q_rows_alloc + p.q_row0 + i] * 1.4426950408889634f;
+      p.ndelta[w] = -s;
+      p.nlse2[w] = p.lse[bh * p.q_rows_alloc + p.q_row0 + i] * -1.4426950408889634f;
     } else {  // padding row of the last tile
-      p.delta[w] = 0.f;
-      p.lse2[w] = INFINITY;
+      p.ndelta[w] = 0.f;
+      p.nlse2[w] = -INFINITY;
     }
   }
 }
@@ -260,12 +266,27 @@ struct BwdConfig {
   static constexpr int Q_DQ = 2 * Q_KT;
   static constexpr uint32_t Q_TMEM = tmem_cols_for(Q_DQ + HD);
   __host__ __device__ static constexpr int q_dp(int b) { return Q_KT + b * Q_KT; }
+  // dK/dV kernel, 16-bit I/O: the per-query rows (nlse2, ndelta) of each
+  // streamed query tile, staged by the TMA warp in a ring of LD_SLOTS slots
+  // (each 2 x KV_QT floats) and released by the compute warps after the
+  // tile's dS pass, so that the compute warps read them from shared memory
+  // instead of L2, and form P / dS with packed fp32x2 FMAs, adds and
+  // multiplies, the softmax scale applied to dK in the epilogue (config 3:
+  // dK/dV 0.712 -> 0.69 ms).  tf32 keeps its rows in registers, loaded from
+  // L2 before each S^T wait, and scalar math: its four compute warpgroups
+  // run at 96 registers (five warps per SM sub-partition), and the ring and
+  // packed forms measured ~4 % slower there (0.089 -> 0.093 ms at config 2).
+  static constexpr bool ROWS_RING = !TF32;
+  static constexpr int LD_SLOTS = 4;
+  static constexpr int LD_BYTES = 2 * KV_QT * 4;
   static constexpr int NUM_BARS = 32;
-  static constexpr int KV_SMEM = 1024 + 2 * BIG_TILE + KV_ST * KV_STAGE_BYTES + NUM_BARS * 8 + 16;
+  static constexpr int KV_SMEM =
+      1024 + 2 * BIG_TILE + KV_ST * KV_STAGE_BYTES + (ROWS_RING ? LD_SLOTS * LD_BYTES : 0) + NUM_BARS * 8 + 16;
   static constexpr int Q_SMEM = 1024 + 2 * BIG_TILE + Q_KST * Q_KSTAGE_BYTES + Q_VST * Q_VSTAGE_BYTES + NUM_BARS * 8 + 16;
   static constexpr int THREADS = 320;  // dQ kernel: 8 compute warps, TMA warp, MMA warp
   static_assert(KV_ST >= 1 && Q_KST >= 1 && Q_VST >= 1, "shared memory budget");
-  static_assert(10 + 2 * KV_PARTS * KV_ST <= NUM_BARS, "dK/dV kernel barriers");
+  static_assert(10 + 2 * KV_PARTS * KV_ST + 2 * LD_SLOTS <= NUM_BARS, "dK/dV kernel barriers");
+  static_assert(KV_SMEM <= 232448, "dK/dV kernel shared memory");
   static_assert(Q_SMEM <= 232448, "dQ kernel shared memory");
   static_assert(KV_DV + HD <= 512 && Q_DQ + HD <= 512, "TMEM budget");
   static_assert(HD * EB % 128 == 0, "head dim must fill whole 128-byte rows");
@@ -322,11 +343,11 @@ __device__ __forceinline__ void tmem_store_operand(uint32_t taddr, const float (
   }
 }
 
-// Add `COLS` fp32 TMEM columns of this thread's lane into a row of an fp32
-// buffer (the block entry points accumulate over ring steps; each CTA owns its
-// rows within one launch, so no atomics).
+// Add `COLS` fp32 TMEM columns of this thread's lane, times `mul`, into a row
+// of an fp32 buffer (the block entry points accumulate over ring steps; each
+// CTA owns its rows within one launch, so no atomics).
 template <int COLS>
-__device__ __forceinline__ void tmem_row_accumulate(uint32_t taddr, float* dst, bool store) {
+__device__ __forceinline__ void tmem_row_accumulate(uint32_t taddr, float* dst, bool store, float mul) {
 #pragma unroll
   for (int c = 0; c < COLS / 32; ++c) {
     uint32_t regs[32];
@@ -337,25 +358,29 @@ __device__ __forceinline__ void tmem_row_accumulate(uint32_t taddr, float* dst, 
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       float4 a = d4[i];
-      a.x += __uint_as_float(regs[4 * i]);
-      a.y += __uint_as_float(regs[4 * i + 1]);
-      a.z += __uint_as_float(regs[4 * i + 2]);
-      a.w += __uint_as_float(regs[4 * i + 3]);
+      a.x = fmaf(__uint_as_float(regs[4 * i]), mul, a.x);
+      a.y = fmaf(__uint_as_float(regs[4 * i + 1]), mul, a.y);
+      a.z = fmaf(__uint_as_float(regs[4 * i + 2]), mul, a.z);
+      a.w = fmaf(__uint_as_float(regs[4 * i + 3]), mul, a.w);
       d4[i] = a;
     }
   }
 }
 
-// Write `cols` (multiple of 32) fp32 TMEM columns of this thread's lane to a
-// row of DT in global memory (zeros when `zero`).
+// Write `cols` (multiple of 32) fp32 TMEM columns of this thread's lane, times
+// `mul`, to a row of DT in global memory (zeros when `zero`).
 template <typename DT, int COLS>
-__device__ __forceinline__ void tmem_row_to_global(uint32_t taddr, DT* dst, bool store, bool zero) {
+__device__ __forceinline__ void tmem_row_to_global(uint32_t taddr, DT* dst, bool store, bool zero, float mul) {
 #pragma unroll
   for (int c = 0; c < COLS / 32; ++c) {
     uint32_t regs[32];
     if (!zero) {
       tmem_ld32(taddr + c * 32, regs);
       tmem_wait_ld();
+      if (mul != 1.f) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) regs[i] = __float_as_uint(__uint_as_float(regs[i]) * mul);
+      }
     } else {
 #pragma unroll
       for (int i = 0; i < 32; ++i) regs[i] = 0u;
@@ -466,7 +491,11 @@ __global__ void __launch_bounds__(BwdConfig<DT, HD>::KV_THREADS, 1)
   auto sdO = [&](int st) { return sStage + st * C::KV_STAGE_BYTES + C::KV_QTILE; };
   auto sQm = [&](int st) { return C::TF32 ? sStage + st * C::KV_STAGE_BYTES + 2 * C::KV_QTILE : sQ(st); };
   auto sdOm = [&](int st) { return C::TF32 ? sStage + st * C::KV_STAGE_BYTES + 3 * C::KV_QTILE : sdO(st); };
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + ST * C::KV_STAGE_BYTES);
+  // per-query rows of the streamed tiles: slot l = nlse2[QT] | ndelta[QT]
+  float* sRows = reinterpret_cast<float*>(sStage + ST * C::KV_STAGE_BYTES);
+  constexpr int LDS = C::LD_SLOTS;
+  uint64_t* bars =
+      reinterpret_cast<uint64_t*>(sStage + ST * C::KV_STAGE_BYTES + (C::ROWS_RING ? LDS * C::LD_BYTES : 0));
   uint64_t* kv_full = bars;
   uint64_t* kv_empty = kv_full + 1;
   constexpr int NP = C::KV_PARTS;
@@ -482,7 +511,9 @@ __global__ void __launch_bounds__(BwdConfig<DT, HD>::KV_THREADS, 1)
   uint64_t* acc_full = pt_full + 1;
   uint64_t* acc_free = acc_full + 1;
   uint64_t* done_bar = acc_free + 1;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done_bar + 1);
+  uint64_t* rows_full = done_bar + 1;     // [LDS]
+  uint64_t* rows_empty = rows_full + LDS;  // [LDS]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(rows_empty + LDS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -517,6 +548,10 @@ __global__ void __launch_bounds__(BwdConfig<DT, HD>::KV_THREADS, 1)
     mbar_init(acc_full, 1);
     mbar_init(acc_free, CT);
     mbar_init(done_bar, 1);
+    for (int l = 0; l < LDS; ++l) {
+      mbar_init(&rows_full[l], 1);
+      mbar_init(&rows_empty[l], CW);  // one arrival per compute warp
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -542,6 +577,7 @@ __global__ void __launch_bounds__(BwdConfig<DT, HD>::KV_THREADS, 1)
       int issued[NP];  // query tiles whose part q was issued
 #pragma unroll
       for (int q = 0; q < NP; ++q) issued[q] = 0;
+      int issued_rows = 0;
       bool ok = true;
       for (int r = 0; ok; ++r) {
         const int w = snake_item(r, cta, G);
@@ -563,6 +599,15 @@ __global__ void __launch_bounds__(BwdConfig<DT, HD>::KV_THREADS, 1)
         for (int it = 0; ok && it < n_it; ++it, ++g) {
           const int st = g % ST;
           const int row = p.q_row0 + (qt_first + it) * QT;
+          if constexpr (C::ROWS_RING) {  // the tile's nlse2 / ndelta rows (QT floats each, 16-byte aligned: Tq_pad is whole tiles)
+            const int l = g % LDS;
+            if (!(ok = mbar_wait(&rows_empty[l], ((g / LDS) & 1) ^ 1, abort_flag, limit, 48))) break;
+            const size_t off = (size_t)bh * p.Tq_pad + (size_t)(qt_first + it) * QT;
+            mbar_arrive_expect_tx(&rows_full[l], C::LD_BYTES);
+            bulk_load_1d(sRows + l * 2 * QT, p.nlse2 + off, QT * 4, &rows_full[l]);
+            bulk_load_1d(sRows + l * 2 * QT + QT, p.ndelta + off, QT * 4, &rows_full[l]);
+            issued_rows = g + 1;
+          }
           // parts in the order the GEMMs read them
 #pragma unroll
           for (int q = 0; q < NP; ++q) {
@@ -598,6 +643,10 @@ __global__ void __launch_bounds__(BwdConfig<DT, HD>::KV_THREADS, 1)
         for (int q = 0; q < NP; ++q)
           for (int it = max(0, issued[q] - ST); it < issued[q]; ++it)
             while (!mbar_try_wait(pfull(q, it % ST), (it / ST) & 1) && globaltimer_ns() - t0 < limit) {
+            }
+        if constexpr (C::ROWS_RING)
+          for (int it = max(0, issued_rows - LDS); it < issued_rows; ++it)
+            while (!mbar_try_wait(&rows_full[it % LDS], (it / LDS) & 1) && globaltimer_ns() - t0 < limit) {
             }
       }
     }
@@ -765,21 +814,31 @@ __global__ void __launch_bounds__(BwdConfig<DT, HD>::KV_THREADS, 1)
         }
         continue;
       }
-      // lse*log2(e) and delta for this head, padded to whole tiles (+inf / 0 on
-      // padding rows), 16-byte aligned: whole float4 loads, no bounds checks.
-      const float* lse2_bh = p.lse2 + (size_t)bh * p.Tq_pad;
-      const float* delta_bh = p.delta + (size_t)bh * p.Tq_pad;
       for (int it = 0; it < n_it; ++it, ++g) {
         const int qtile0 = (qt_first + it) * QT;
         const int q0 = qtile0 + h * HALF;
-        float L[HALF];
+        // this tile's -lse*log2(e) and -delta rows (padded to whole tiles: -inf
+        // / 0 on padding rows): 16-bit from the shared-memory ring the TMA warp
+        // fills; tf32 from L2, -lse*log2(e) into registers before the S^T wait
+        const int l = g % LDS;
+        const float4* nL4;
+        const float4* nD4;
+        float nLr[C::ROWS_RING ? 4 : HALF];
+        if constexpr (C::ROWS_RING) {
+          if (!(ok = mbar_wait(&rows_full[l], (g / LDS) & 1, abort_flag, limit, 49))) break;
+          nL4 = reinterpret_cast<const float4*>(sRows + l * 2 * QT + h * HALF);
+          nD4 = reinterpret_cast<const float4*>(sRows + l * 2 * QT + QT + h * HALF);
+        } else {
+          nL4 = reinterpret_cast<const float4*>(p.nlse2 + (size_t)bh * p.Tq_pad + q0);
+          nD4 = reinterpret_cast<const float4*>(p.ndelta + (size_t)bh * p.Tq_pad + q0);
 #pragma unroll
-        for (int c = 0; c < HALF / 4; ++c) {
-          const float4 v4 = __ldg(reinterpret_cast<const float4*>(lse2_bh + q0) + c);
-          L[4 * c] = v4.x;
-          L[4 * c + 1] = v4.y;
-          L[4 * c + 2] = v4.z;
-          L[4 * c + 3] = v4.w;
+          for (int c = 0; c < HALF / 4; ++c) {
+            const float4 v4 = __ldg(nL4 + c);
+            nLr[4 * c] = v4.x;
+            nLr[4 * c + 1] = v4.y;
+            nLr[4 * c + 2] = v4.z;
+            nLr[4 * c + 3] = v4.w;
+          }
         }
         if (!(ok = mbar_wait(s_full, g & 1, abort_flag, limit, 17))) break;
         tc_fence_after();
@@ -787,9 +846,24 @@ __global__ void __launch_bounds__(BwdConfig<DT, HD>::KV_THREADS, 1)
         tmem_load_row(tbase + lane_off + C::KV_S + h * HALF, sv);
         tc_fence_before();
         mbar_arrive(s_free);
-        // P^T = exp2(S^T * scale*log2e - lse*log2e); padding queries have lse = +inf
+        // P^T = exp2(S^T * scale*log2e - lse*log2e); padding queries have
+        // -lse*log2e = -inf, so P = 0
+        if constexpr (!C::ROWS_RING) {
 #pragma unroll
-        for (int c = 0; c < HALF; ++c) sv[c] = ex2_approx(fmaf(sv[c], sl2, -L[c]));
+          for (int c = 0; c < HALF; ++c) sv[c] = ex2_approx(fmaf(sv[c], sl2, nLr[c]));
+        } else {  // two columns per packed FMA
+          const float2 sl2x2 = make_float2(sl2, sl2);
+#pragma unroll
+          for (int c = 0; c < HALF; c += 4) {
+            const float4 n4 = nL4[c / 4];  // shared-memory broadcast: every lane reads the same row
+            const float2 y0 = __ffma2_rn(make_float2(sv[c], sv[c + 1]), sl2x2, make_float2(n4.x, n4.y));
+            const float2 y1 = __ffma2_rn(make_float2(sv[c + 2], sv[c + 3]), sl2x2, make_float2(n4.z, n4.w));
+            sv[c] = ex2_approx(y0.x);
+            sv[c + 1] = ex2_approx(y0.y);
+            sv[c + 2] = ex2_approx(y1.x);
+            sv[c + 3] = ex2_approx(y1.y);
+          }
+        }
         // causal diagonal tile / keys past Tk: zero the invisible entries
         if (!key_ok) {
 #pragma unroll
@@ -810,8 +884,10 @@ __global__ void __launch_bounds__(BwdConfig<DT, HD>::KV_THREADS, 1)
         }
         if (!(ok = mbar_wait(dp_full, g & 1, abort_flag, limit, 18))) break;
         tc_fence_after();
-        // dS^T = P^T (dP^T - delta) * scale, 32 columns at a time, written in
-        // place (tf32) or packed into the already-read front of the dP buffer.
+        // dS^T = P^T (dP^T - delta) (tf32: times the softmax scale; 16-bit:
+        // packed adds / multiplies, the scale goes on dK in the epilogue), 32
+        // columns at a time, written in place (tf32) or packed into the
+        // already-read front of the dP buffer.
 #pragma unroll
         for (int ch = 0; ch < HALF / 32; ++ch) {
           float dsv[32];
@@ -821,19 +897,37 @@ __global__ void __launch_bounds__(BwdConfig<DT, HD>::KV_THREADS, 1)
             tmem_wait_ld();
 #pragma unroll
             for (int c4 = 0; c4 < 8; ++c4) {
-              const float4 d4 = __ldg(reinterpret_cast<const float4*>(delta_bh + q0 + ch * 32) + c4);
-              const float dd[4] = {d4.x, d4.y, d4.z, d4.w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int i = 4 * c4 + e;
-                dsv[i] = sv[ch * 32 + i] * (__uint_as_float(regs[i]) - dd[e]) * scale;
+              const int i = 4 * c4;
+              if constexpr (!C::ROWS_RING) {
+                const float4 d4 = __ldg(nD4 + ch * 8 + c4);
+                dsv[i] = sv[ch * 32 + i] * (__uint_as_float(regs[i]) + d4.x) * scale;
+                dsv[i + 1] = sv[ch * 32 + i + 1] * (__uint_as_float(regs[i + 1]) + d4.y) * scale;
+                dsv[i + 2] = sv[ch * 32 + i + 2] * (__uint_as_float(regs[i + 2]) + d4.z) * scale;
+                dsv[i + 3] = sv[ch * 32 + i + 3] * (__uint_as_float(regs[i + 3]) + d4.w) * scale;
+                continue;
               }
+              const float4 d4 = nD4[ch * 8 + c4];
+              const float2 t0 = __fadd2_rn(make_float2(__uint_as_float(regs[i]), __uint_as_float(regs[i + 1])),
+                                           make_float2(d4.x, d4.y));
+              const float2 t1 = __fadd2_rn(make_float2(__uint_as_float(regs[i + 2]), __uint_as_float(regs[i + 3])),
+                                           make_float2(d4.z, d4.w));
+              const float2 r0 = __fmul2_rn(make_float2(sv[ch * 32 + i], sv[ch * 32 + i + 1]), t0);
+              const float2 r1 = __fmul2_rn(make_float2(sv[ch * 32 + i + 2], sv[ch * 32 + i + 3]), t1);
+              dsv[i] = r0.x;
+              dsv[i + 1] = r0.y;
+              dsv[i + 2] = r1.x;
+              dsv[i + 3] = r1.y;
             }
           }
           if constexpr (C::TF32)
             tmem_store_operand<DT>(tbase + lane_off + C::KV_DP + h * HALF + ch * 32, dsv);
           else
             tmem_store_operand<DT>(tbase + lane_off + C::KV_DP + h * HALF + ch * 16, dsv);
+        }
+        // the tile's rows in shared memory are no longer read by this warp
+        if constexpr (C::ROWS_RING) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&rows_empty[l]);
         }
         if constexpr (!C::EARLY_P) tmem_store_operand<DT>(tbase + lane_off + C::kv_p() + h * HALF, sv);
         tmem_wait_st();
@@ -849,20 +943,21 @@ __global__ void __launch_bounds__(BwdConfig<DT, HD>::KV_THREADS, 1)
         const uint32_t src = tbase + lane_off + (h < 2 ? C::KV_DK : C::KV_DV) + (h & 1) * 32;
         void* dst_row = reinterpret_cast<char*>(h < 2 ? p.dk : p.dv) +
                         (row_index * HD + (h & 1) * 32) * (p.accumulate ? sizeof(float) : sizeof(DT));
+        const float mul = 1.f;  // (tf32: dS^T carries the softmax scale)
         if (p.accumulate)
-          tmem_row_accumulate<32>(src, reinterpret_cast<float*>(dst_row), key_ok);
+          tmem_row_accumulate<32>(src, reinterpret_cast<float*>(dst_row), key_ok, mul);
         else
-          tmem_row_to_global<DT, 32>(src, reinterpret_cast<DT*>(dst_row), key_ok, false);
+          tmem_row_to_global<DT, 32>(src, reinterpret_cast<DT*>(dst_row), key_ok, false, mul);
       } else if (p.accumulate) {
         tmem_row_accumulate<HD / 2>(tbase + lane_off + C::KV_DK + col,
-                                    reinterpret_cast<float*>(p.dk) + row_index * HD + col, key_ok);
+                                    reinterpret_cast<float*>(p.dk) + row_index * HD + col, key_ok, scale);
         tmem_row_accumulate<HD / 2>(tbase + lane_off + C::KV_DV + col,
-                                    reinterpret_cast<float*>(p.dv) + row_index * HD + col, key_ok);
+                                    reinterpret_cast<float*>(p.dv) + row_index * HD + col, key_ok, 1.f);
       } else {
         tmem_row_to_global<DT, HD / 2>(tbase + lane_off + C::KV_DK + col,
-                                       reinterpret_cast<DT*>(p.dk) + row_index * HD + col, key_ok, false);
+                                       reinterpret_cast<DT*>(p.dk) + row_index * HD + col, key_ok, false, scale);
         tmem_row_to_global<DT, HD / 2>(tbase + lane_off + C::KV_DV + col,
-                                       reinterpret_cast<DT*>(p.dv) + row_index * HD + col, key_ok, false);
+                                       reinterpret_cast<DT*>(p.dv) + row_index * HD + col, key_ok, false, 1.f);
       }
       tc_fence_before();
       mbar_arrive(acc_free);
@@ -1159,8 +1254,9 @@ __global__ void __launch_bounds__(320, 1)
         }
         continue;
       }
-      const float L = q_ok ? p.lse2[(size_t)bh * p.Tq_pad + q] : 0.f;
-      const float dl = q_ok ? p.delta[(size_t)bh * p.Tq_pad + q] : 0.f;
+      const float nL = q_ok ? p.nlse2[(size_t)bh * p.Tq_pad + q] : 0.f;  // -lse * log2(e)
+      const float nd = q_ok ? p.ndelta[(size_t)bh * p.Tq_pad + q] : 0.f;  // -delta
+      const float2 sl2x2 = make_float2(sl2, sl2), nL2 = make_float2(nL, nL), nd2 = make_float2(nd, nd);
       int vis = p.Tk - 1;
       if (p.causal) vis = min(vis, q + p.causal_offset);
       if (!q_ok) vis = -1;
@@ -1174,7 +1270,11 @@ __global__ void __launch_bounds__(320, 1)
         mbar_arrive(s_free);
         const int lim = vis - kc0;  // columns > lim are masked (diagonal / tail tiles only)
 #pragma unroll
-        for (int c = 0; c < HALF; ++c) sv[c] = ex2_approx(fmaf(sv[c], sl2, -L));
+        for (int c = 0; c < HALF; c += 2) {
+          const float2 y = __ffma2_rn(make_float2(sv[c], sv[c + 1]), sl2x2, nL2);
+          sv[c] = ex2_approx(y.x);
+          sv[c + 1] = ex2_approx(y.y);
+        }
         if (lim < HALF - 1) {
 #pragma unroll
           for (int c = 0; c < HALF; ++c)
@@ -1185,7 +1285,12 @@ __global__ void __launch_bounds__(320, 1)
         float dsv[HALF];
         tmem_load_row(tbase + lane_off + C::q_dp(0) + h * HALF, dsv);
 #pragma unroll
-        for (int c = 0; c < HALF; ++c) dsv[c] = sv[c] * (dsv[c] - dl) * scale;
+        for (int c = 0; c < HALF; c += 2) {  // dS = P (dP - delta); the scale goes on dQ in the epilogue
+          const float2 r = __fmul2_rn(make_float2(sv[c], sv[c + 1]),
+                                      __fadd2_rn(make_float2(dsv[c], dsv[c + 1]), nd2));
+          dsv[c] = r.x;
+          dsv[c + 1] = r.y;
+        }
         tmem_store_operand<DT>(tbase + lane_off + C::q_dp(0) + h * HALF, dsv);
         tmem_wait_st();
         tc_fence_before();
@@ -1199,6 +1304,8 @@ __global__ void __launch_bounds__(320, 1)
       tmem_row_load<HD / 2>(tbase + lane_off + C::Q_DQ + col, acc);
       tc_fence_before();
       mbar_arrive(acc_free);
+#pragma unroll
+      for (int i = 0; i < HD / 2; ++i) acc[i] = __float_as_uint(__uint_as_float(acc[i]) * scale);
       if (q_ok) {
         if (p.accumulate)
           row_store<DT, HD / 2>(acc, reinterpret_cast<float*>(p.dq) + lrow * HD + col, true);

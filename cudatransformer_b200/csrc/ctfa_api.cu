@@ -365,7 +365,7 @@ size_t padded_rows(const Problem& pr) { return (size_t)pr.B * pr.H * padded_tq(p
 size_t bwd_workspace(const Problem& pr) {
   const size_t rows = (size_t)pr.B * pr.H * pr.Tq;
   if (tensor_core_shape(pr) && !(pr.D == 128 && (pr.dtype == CTFA_DTYPE_F32 || pr.dtype == CTFA_DTYPE_TF32))) {
-    size_t ws = 2 * align256(padded_rows(pr) * sizeof(float));  // delta, lse*log2(e) (padded rows)
+    size_t ws = 2 * align256(padded_rows(pr) * sizeof(float));  // -delta, -lse*log2(e) (padded rows)
     const size_t n = align256(rows * pr.D * sizeof(float));
     if (pr.dtype == CTFA_DTYPE_F32) ws += 4 * n;   // rounded q, k, v, dO
     if (pr.dtype == CTFA_DTYPE_TF32) ws += n;      // rounded dO
@@ -412,21 +412,21 @@ int launch_bwd_tc(const Problem& pr, const void* q, const void* k, const void* v
                   cudaEvent_t* ev) {
   using C = BwdConfig<DT, HD>;
   const int BH = pr.B * pr.H;
-  float* delta = reinterpret_cast<float*>(ws);
-  // 1. delta = rowsum(O * dO)
+  float* ndelta = reinterpret_cast<float*>(ws);
+  // 1. -delta = -rowsum(O * dO), and -lse * log2(e)
   const int Tq_pad = (int)padded_tq(pr);
-  float* lse2 = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + align256(padded_rows(pr) * sizeof(float)));
+  float* nlse2 = reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + align256(padded_rows(pr) * sizeof(float)));
   BwdPrepParams pp;
   pp.rows = (long long)BH * Tq_pad;
   pp.Tq = pr.Tq;
   pp.Tq_pad = Tq_pad;
   pp.lse = lse;
-  pp.lse2 = lse2;
+  pp.nlse2 = nlse2;
   pp.q_rows_alloc = pr.q_rows;
   pp.q_row0 = pr.q_row0;
   pp.o = o;
   pp.dO = dO;
-  pp.delta = delta;
+  pp.ndelta = ndelta;
   pp.dO_round = (dO_mma != dO) ? reinterpret_cast<float*>(const_cast<void*>(dO_mma)) : nullptr;
   if (!std::is_same<DT, float>::value) record(ev, 0, stream);
   const long long prep_blocks =
@@ -470,8 +470,8 @@ int launch_bwd_tc(const Problem& pr, const void* q, const void* k, const void* v
   p.scale = (float)(1.0 / std::sqrt((double)HD));
   p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)HD));
   p.Tq_pad = Tq_pad;
-  p.lse2 = lse2;
-  p.delta = delta;
+  p.nlse2 = nlse2;
+  p.ndelta = ndelta;
   p.dq = dq;
   p.dk = dk;
   p.dv = dv;

@@ -141,6 +141,17 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap, ui
       : "memory");
 }
 
+// Plain (untiled) bulk copy of `bytes` contiguous bytes from global to shared
+// memory, completing on `bar` like a tensor load.  Both addresses 16-byte
+// aligned, `bytes` a multiple of 16.
+__device__ __forceinline__ void bulk_load_1d(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Store a shared-memory tile to global memory through a tensor map (bulk
 // group).  Coordinates are never negative here; rows past the tensor's extent
 // are clipped by the copy engine.

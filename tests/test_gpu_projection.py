@@ -19,8 +19,9 @@ TOL = {torch.float32: 2e-3, torch.bfloat16: 1e-2, torch.float16: 1e-2, torch.flo
 
 # (B, T, E, H, D): config-4 block shape; ragged T with H*D % 128 = 64; D = 128;
 # E not a multiple of 128 (fp32: tensor cores, 16-bit: SIMT since E*2 % 16 != 0);
-# one sequence shorter than a tile
-SHAPES = [(2, 256, 384, 6, 64), (3, 200, 192, 3, 64), (2, 77, 256, 2, 128), (1, 130, 100, 2, 64), (2, 9, 64, 1, 64)]
+# one sequence shorter than a tile; one-token sequences
+SHAPES = [(2, 256, 384, 6, 64), (3, 200, 192, 3, 64), (2, 77, 256, 2, 128), (1, 130, 100, 2, 64), (2, 9, 64, 1, 64),
+          (1, 1, 384, 6, 64), (3, 1, 128, 2, 128)]
 
 
 def _inputs(B, T, E, H, D, dt, dev, seed):
