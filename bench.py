@@ -317,10 +317,11 @@ def run_ring(args, w, rank, world, local):
     for _ in range(args.warmup):
         e2e_step()
     ms_e2e = timed(e2e_step, args.steps)
-    # kernel launches per step: forward = block kernel + merge per block, backward = delta pass +
-    # dK/dV + dQ per block; plus per-step zeroing / accumulation and the final conversions
+    # kernel launches per step: forward = one block kernel per block (the merge is in its epilogue),
+    # backward = delta pass + dK/dV + dQ per block; plus per-step zeroing / accumulation and the final
+    # conversions
     n_blocks = sum(len(ra.block_plan(world, rank, s)) for s in range(world))
-    launches = 2 * n_blocks + 3 * n_blocks + 2 * world + 4
+    launches = n_blocks + 3 * n_blocks + 2 * world + 4
     total = path_flops(B, H, T, D, True)
     peaks = measured_peaks()
     peak = float(peaks.get("bf16_tflops", 1590.0))

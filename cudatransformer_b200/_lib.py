@@ -60,6 +60,7 @@ SIGNATURES = {
         [_c_void_p] * 9 + [_c_int] * 6 + [_c_void_p],
     ),
     "ctfa_forward_block": (_c_int, [_c_void_p] * 5 + [_c_int] * 12 + [_c_void_p]),
+    "ctfa_forward_block_merge": (_c_int, [_c_void_p] * 5 + [_c_int] * 13 + [_c_void_p]),
     "ctfa_merge_blocks": (_c_int, [_c_void_p] * 4 + [_c_int] * 7 + [_c_void_p]),
     "ctfa_convert_f32": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_size_t, _c_void_p]),
     "ctfa_backward_block_workspace_bytes": (_c_size_t, [_c_int] * 5),

@@ -57,6 +57,8 @@ struct FwdParams {
   void* o;             // [BH][q_rows_alloc][HD] DT
   float* o_f32;        // when set: fp32 output rows here instead of o (block partials)
   float* lse;          // [BH][q_rows_alloc] natural-log logsumexp (nullable)
+  int merge;           // with o_f32: o_f32 / lse hold a running (o, lse) of earlier key blocks,
+                       // which this block is folded into (logsumexp-weighted) instead of overwriting
   unsigned long long wait_limit_ns;
 };
 
@@ -572,16 +574,49 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
       DT* orow = reinterpret_cast<DT*>(p.o) + row_index * HD;
       float* orow32 = p.o_f32 != nullptr ? p.o_f32 + row_index * HD : nullptr;
 #pragma unroll
+      // this block's logsumexp; with `merge`, the row's running (o, lse) and
+      // this block's are combined as o = ca * o_run + cb * O with
+      // ca = e^(lse_run - lse_new), cb = e^(lse_blk - lse_new) / l
+      const float lse_blk = l > 0.f ? (((m == -INFINITY) ? 0.f : m) + __log2f(l)) * 0.69314718055994531f : -INFINITY;
+      float ca = 0.f, cb = inv_l, lse_new = lse_blk;
+      bool keep = false;  // no visible key in either: leave the running row as it is
+      if (p.merge && row_ok && orow32 != nullptr) {
+        const float lse_run = p.lse[row_index];
+        const float mx = fmaxf(lse_run, lse_blk);
+        if (mx == -INFINITY) {
+          keep = true;
+        } else {
+          const float wa = __expf(lse_run - mx), wb = __expf(lse_blk - mx);
+          const float inv = 1.f / (wa + wb);
+          ca = wa * inv;
+          cb = wb * inv * inv_l;
+          lse_new = mx + __logf(wa + wb);
+        }
+      }
+#pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t regs[32];
         tmem_ld32(o_addr + c * 32, regs);
         tmem_wait_ld();
         if (row_ok && orow32 != nullptr) {
           float4* dst = reinterpret_cast<float4*>(orow32 + c * 32);
+          if (keep) continue;
+          if (p.merge) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            dst[i] = make_float4(__uint_as_float(regs[4 * i]) * inv_l, __uint_as_float(regs[4 * i + 1]) * inv_l,
-                                 __uint_as_float(regs[4 * i + 2]) * inv_l, __uint_as_float(regs[4 * i + 3]) * inv_l);
+            for (int i = 0; i < 8; ++i) {
+              const float4 a = dst[i];
+              dst[i] = make_float4(fmaf(a.x, ca, __uint_as_float(regs[4 * i]) * cb),
+                                   fmaf(a.y, ca, __uint_as_float(regs[4 * i + 1]) * cb),
+                                   fmaf(a.z, ca, __uint_as_float(regs[4 * i + 2]) * cb),
+                                   fmaf(a.w, ca, __uint_as_float(regs[4 * i + 3]) * cb));
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              dst[i] = make_float4(__uint_as_float(regs[4 * i]) * inv_l, __uint_as_float(regs[4 * i + 1]) * inv_l,
+                                   __uint_as_float(regs[4 * i + 2]) * inv_l,
+                                   __uint_as_float(regs[4 * i + 3]) * inv_l);
+          }
         } else if (row_ok) {
           if constexpr (C::EB == 4) {
             float4* dst = reinterpret_cast<float4*>(orow + c * 32);
@@ -606,10 +641,7 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
           }
         }
       }
-      if (row_ok && p.lse != nullptr) {
-        const float m_use = (m == -INFINITY) ? 0.f : m;
-        p.lse[row_index] = l > 0.f ? (m_use + __log2f(l)) * 0.69314718055994531f : -INFINITY;
-      }
+      if (row_ok && p.lse != nullptr && !keep) p.lse[row_index] = lse_new;
     }
     if (q_stored) tma_store_wait_all();
   }

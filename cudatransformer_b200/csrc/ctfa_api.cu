@@ -127,6 +127,7 @@ struct Problem {
   int q_row0, k_row0;
   int causal, causal_offset;
   float* o_f32 = nullptr;  // forward: fp32 output rows instead of o (block partials)
+  int merge = 0;           // forward with o_f32: fold into the running (o_f32, lse) instead of overwriting
   int accumulate = 0;      // backward: add into fp32 dq/dk/dv instead of writing the I/O type
 };
 
@@ -171,6 +172,7 @@ int launch_fwd_tc(const Problem& pr, const void* q, const void* k, const void* v
   p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)HD));
   p.o = o;
   p.o_f32 = pr.o_f32;
+  p.merge = pr.merge;
   p.lse = lse;
   p.wait_limit_ns = g_wait_limit_ns;
   auto kern = attn_fwd_sm100<DT, HD, NQ, BN, KST, VST, RND>;
@@ -806,6 +808,18 @@ extern "C" int ctfa_forward_block(const void* q, const void* k, const void* v, f
   Problem pr = block_problem(B, H, D, dtype, q_rows, q_row0, Tq, k_rows, k_row0, Tk, causal, causal_offset);
   pr.o_f32 = o_blk;
   return forward_impl(pr, q, k, v, o_blk, lse_blk, nullptr, (cudaStream_t)stream);
+}
+
+extern "C" int ctfa_forward_block_merge(const void* q, const void* k, const void* v, float* o_acc, float* lse_acc,
+                                        int B, int H, int D, int dtype, int q_rows, int q_row0, int Tq, int k_rows,
+                                        int k_row0, int Tk, int causal, int causal_offset, int init, void* stream) {
+  int s = check_block(q, k, v, B, H, D, dtype, q_rows, q_row0, Tq, k_rows, k_row0, Tk);
+  if (s != CTFA_OK) return s;
+  if (!o_acc || !lse_acc) return fail(CTFA_ERR_INVALID_ARGUMENT, "o_acc and lse_acc must be non-null");
+  Problem pr = block_problem(B, H, D, dtype, q_rows, q_row0, Tq, k_rows, k_row0, Tk, causal, causal_offset);
+  pr.o_f32 = o_acc;
+  pr.merge = init ? 0 : 1;
+  return forward_impl(pr, q, k, v, o_acc, lse_acc, nullptr, (cudaStream_t)stream);
 }
 
 extern "C" int ctfa_merge_blocks(float* o_acc, float* lse_acc, const float* o_blk, const float* lse_blk, int B,

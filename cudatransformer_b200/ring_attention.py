@@ -14,8 +14,10 @@ Forward, step s = 0..G-1: rank r holds the k/v of rank src = (r - s) mod G.
 For each local query chunk a and held key chunk b (global chunk ids): b < a
 is a full block, b == a the causal diagonal, b > a is skipped.  Each block's
 normalised output and logsumexp are folded into fp32 accumulators with a
-logsumexp-weighted merge.  The next k/v block is sent/received (one batched
-NCCL send+recv) while the current one is computed.
+logsumexp-weighted merge, done in the block kernel's epilogue
+(ctfa_forward_block_merge: no per-block partial goes through HBM).  The next
+k/v block is sent/received (one batched NCCL send+recv) while the current one
+is computed.
 
 Backward: the same schedule; dq accumulates locally, dK/dV contributions for
 the held block accumulate in a fresh buffer, are added to the partial sums
@@ -25,9 +27,9 @@ pair is identical on both sides (k/v at the start of steps 0..G-2, dK/dV at
 the end of steps 0..G-1), so NCCL matches every message.
 
 The per-block compute is an injected ``ops`` object: ``CudaBlockOps`` calls
-the tcgen05 kernels through the C ABI (ctfa_forward_block,
-ctfa_merge_blocks, ctfa_backward_block, ctfa_convert_f32); tests plug in a
-CPU implementation to check the schedule on gloo ranks.
+the tcgen05 kernels through the C ABI (ctfa_forward_block_merge,
+ctfa_backward_block, ctfa_convert_f32); tests plug in a CPU implementation to
+check the schedule on gloo ranks.
 """
 from __future__ import annotations
 
@@ -89,6 +91,7 @@ class CudaBlockOps:
 
     def __init__(self):
         self.lib = _lib.load()
+        self._ws = None  # backward block workspace, kept across blocks and calls
 
     @staticmethod
     def _stream(t):
@@ -100,6 +103,15 @@ class CudaBlockOps:
                                                lse_blk.data_ptr(), B, H, D, _CODES[q.dtype], rows, q_row0, n,
                                                k.shape[2], k_row0, n, int(causal), 0, self._stream(q)),
                    "ctfa_forward_block")
+
+    def forward_merge(self, q, k, v, o_acc, lse_acc, q_row0, k_row0, n, causal, init):
+        """Block forward folded into the running (o_acc, lse_acc) rows in the
+        kernel's epilogue (init: the rows' first block, overwritten)."""
+        B, H, rows, D = q.shape
+        _lib.check(self.lib.ctfa_forward_block_merge(q.data_ptr(), k.data_ptr(), v.data_ptr(), o_acc.data_ptr(),
+                                                     lse_acc.data_ptr(), B, H, D, _CODES[q.dtype], rows, q_row0, n,
+                                                     k.shape[2], k_row0, n, int(causal), 0, int(init),
+                                                     self._stream(q)), "ctfa_forward_block_merge")
 
     def merge(self, o_acc, lse_acc, o_blk, lse_blk, row0, n, init):
         B, H, rows, D = o_acc.shape
@@ -116,8 +128,10 @@ class CudaBlockOps:
     def backward_block(self, q, k, v, o, do, lse, dq_acc, dk_acc, dv_acc, q_row0, k_row0, n, causal):
         B, H, rows, D = q.shape
         code = _CODES[q.dtype]
-        ws_bytes = self.lib.ctfa_backward_block_workspace_bytes(B, H, n, D, code)
-        ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=q.device)
+        ws_bytes = max(self.lib.ctfa_backward_block_workspace_bytes(B, H, n, D, code), 256)
+        if self._ws is None or self._ws.device != q.device or self._ws.numel() < ws_bytes:
+            self._ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+        ws = self._ws  # stream-ordered reuse: the blocks run one after another on one stream
         _lib.check(self.lib.ctfa_backward_block(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), do.data_ptr(),
                                                 lse.data_ptr(), dq_acc.data_ptr(), dk_acc.data_ptr(), dv_acc.data_ptr(),
                                                 ws.data_ptr(), ws.numel(), B, H, D, code, rows, q_row0, n,
@@ -157,16 +171,14 @@ class RingAttention:
         C = rows // 2
         o_acc = torch.zeros((B, H, rows, D), dtype=torch.float32, device=q.device)
         lse_acc = torch.full((B, H, rows), float("-inf"), dtype=torch.float32, device=q.device)
-        o_blk = torch.empty_like(o_acc)
-        lse_blk = torch.empty_like(lse_acc)
         kv = torch.stack([k, v])
         kv_next = torch.empty_like(kv)
         seen = [False, False]
         for step in range(self.world):
             reqs = self._exchange(kv, kv_next) if step + 1 < self.world else []
             for a_loc, b_loc, causal in block_plan(self.world, self.rank, step):
-                self.ops.forward_block(q, kv[0], kv[1], o_blk, lse_blk, a_loc * C, b_loc * C, C, causal)
-                self.ops.merge(o_acc, lse_acc, o_blk, lse_blk, a_loc * C, C, not seen[a_loc])
+                self.ops.forward_merge(q, kv[0], kv[1], o_acc, lse_acc, a_loc * C, b_loc * C, C, causal,
+                                       not seen[a_loc])
                 seen[a_loc] = True
             for r in reqs:
                 r.wait()
@@ -220,13 +232,12 @@ def ring_attention_emulated(q, k, v, do, world: int, ops=None):
     for r in range(world):
         o_acc = torch.zeros((B, H, 2 * C, D), dtype=torch.float32, device=q.device)
         lse_acc = torch.full((B, H, 2 * C), float("-inf"), dtype=torch.float32, device=q.device)
-        o_blk, lse_blk = torch.empty_like(o_acc), torch.empty_like(lse_acc)
         seen = [False, False]
         for step in range(world):
             src = (r - step) % world
             for a_loc, b_loc, causal in block_plan(world, r, step):
-                ops.forward_block(qs[r], ks[src], vs[src], o_blk, lse_blk, a_loc * C, b_loc * C, C, causal)
-                ops.merge(o_acc, lse_acc, o_blk, lse_blk, a_loc * C, C, not seen[a_loc])
+                ops.forward_merge(qs[r], ks[src], vs[src], o_acc, lse_acc, a_loc * C, b_loc * C, C, causal,
+                                  not seen[a_loc])
                 seen[a_loc] = True
         outs.append(ops.finalize(o_acc, q.dtype))
         lses.append(lse_acc)

@@ -153,6 +153,16 @@ int ctfa_forward_block(const void* q, const void* k, const void* v, float* o_blk
                        int D, int dtype, int q_rows, int q_row0, int Tq, int k_rows, int k_row0, int Tk,
                        int causal, int causal_offset, void* stream);
 
+/* ctfa_forward_block with the merge done in the kernel's epilogue: the block's
+ * output is folded straight into the running fp32 (o_acc, lse_acc) of rows
+ * [q_row0, q_row0+Tq) (logsumexp-weighted, as ctfa_merge_blocks does), so no
+ * per-block partial is written and read back.  init = 1: the first block of
+ * those rows (o_acc / lse_acc are overwritten).  Rows with no visible key in
+ * this block or before keep their running values. */
+int ctfa_forward_block_merge(const void* q, const void* k, const void* v, float* o_acc, float* lse_acc, int B,
+                             int H, int D, int dtype, int q_rows, int q_row0, int Tq, int k_rows, int k_row0,
+                             int Tk, int causal, int causal_offset, int init, void* stream);
+
 /* Fold one block's partial (o_blk, lse_blk) into the running (o_acc, lse_acc)
  * on rows [row0, row0+T) of [B, H, rows, *] fp32 buffers: logsumexp-weighted
  * average.  init = 1 copies instead (first block of those rows). */

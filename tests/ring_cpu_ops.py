@@ -26,6 +26,11 @@ class CpuBlockOps:
         o_blk[:, :, q_row0:q_row0 + n] = (torch.exp(s - lse[..., None]) @ vb).to(o_blk.dtype)
         lse_blk[:, :, q_row0:q_row0 + n] = lse.to(lse_blk.dtype)
 
+    def forward_merge(self, q, k, v, o_acc, lse_acc, q_row0, k_row0, n, causal, init):
+        o_blk, lse_blk = torch.empty_like(o_acc), torch.empty_like(lse_acc)
+        self.forward_block(q, k, v, o_blk, lse_blk, q_row0, k_row0, n, causal)
+        self.merge(o_acc, lse_acc, o_blk, lse_blk, q_row0, n, init)
+
     def merge(self, o_acc, lse_acc, o_blk, lse_blk, row0, n, init):
         sl = slice(row0, row0 + n)
         if init:

@@ -1,8 +1,9 @@
 """GPU: ring (sequence-parallel) attention.
 
 * single GPU: the ring schedule for G virtual ranks run on one device through
-  the block entry points (ctfa_forward_block / ctfa_merge_blocks /
-  ctfa_backward_block / ctfa_convert_f32), against fp64 full attention;
+  the block entry points (ctfa_forward_block_merge / ctfa_backward_block /
+  ctfa_convert_f32), against fp64 full attention; and the epilogue merge
+  against the separate block forward + ctfa_merge_blocks;
 * two or more GPUs: the real ring (one process per GPU, NCCL send/recv of K/V
   and dK/dV), gathered and checked the same way.  Skipped with one GPU.
 Tolerance: bf16 I/O, max|x - x64| / max|x64| < 1e-2.
@@ -40,6 +41,42 @@ def test_emulated_ring_block_kernels(cuda_device, world, T, D):
     for name, x in got.items():
         assert orc.max_rel_err(x.double().cpu().numpy(), ref[name]) < 1e-2, name
     assert np.abs(lse.cpu().numpy() - ref["lse"]).max() < 1e-2
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_epilogue_merge_matches_separate_merge(cuda_device, D):
+    """ctfa_forward_block_merge (merge in the kernel's epilogue) against
+    ctfa_forward_block + ctfa_merge_blocks on the same blocks: a first block
+    (init), a full block and a causal diagonal block folded into the same
+    rows, plus rows of a query tile whose causal diagonal leaves early rows
+    with few keys."""
+    ops = ra.CudaBlockOps()
+    B, H, C = 2, 3, 320
+    q, k, v, _ = orc.make_inputs(B, H, 3 * C, D, seed=90 + D)
+    tq, tk, tv = (torch.from_numpy(x).to(cuda_device, torch.bfloat16) for x in (q, k, v))
+    rows = 3 * C
+    runs = {}
+    for mode in ("fused", "separate"):
+        o_acc = torch.zeros((B, H, rows, D), dtype=torch.float32, device=cuda_device)
+        lse_acc = torch.full((B, H, rows), float("-inf"), dtype=torch.float32, device=cuda_device)
+        o_blk, lse_blk = torch.empty_like(o_acc), torch.empty_like(lse_acc)
+        # rows [2C, 3C) see key blocks [0, C) (init), [C, 2C) (full) and [2C, 3C) (causal diagonal)
+        for i, (k0, causal) in enumerate([(0, False), (C, False), (2 * C, True)]):
+            if mode == "fused":
+                ops.forward_merge(tq, tk, tv, o_acc, lse_acc, 2 * C, k0, C, causal, i == 0)
+            else:
+                ops.forward_block(tq, tk, tv, o_blk, lse_blk, 2 * C, k0, C, causal)
+                ops.merge(o_acc, lse_acc, o_blk, lse_blk, 2 * C, C, i == 0)
+        torch.cuda.synchronize()
+        runs[mode] = (o_acc[:, :, 2 * C:].cpu(), lse_acc[:, :, 2 * C:].cpu())
+    (of, lf), (os_, ls_) = runs["fused"], runs["separate"]
+    assert torch.allclose(of, os_, rtol=1e-5, atol=1e-6), (of - os_).abs().max()
+    assert torch.allclose(lf, ls_, rtol=1e-6, atol=1e-5), (lf - ls_).abs().max()
+    # and both are the attention of rows [2C, 3C) over keys [0, 3C) (causal on the last block)
+    qq, kk, vv = (orc.round_to(x, "bf16") for x in (q, k, v))
+    o_ref, lse_ref = orc.attention_f64(qq, kk, vv, True)
+    assert orc.max_rel_err(of.double().numpy(), o_ref[:, :, 2 * C:]) < 1e-2
+    assert np.abs(lf.numpy() - lse_ref[:, :, 2 * C:]).max() < 1e-2
 
 
 def _free_port():
