@@ -317,6 +317,27 @@ def run_ring(args, w, rank, world, local):
     for _ in range(args.warmup):
         e2e_step()
     ms_e2e = timed(e2e_step, args.steps)
+
+    # The same schedule with every exchange replaced by a local device copy of
+    # the same buffers (each rank computes the same blocks on its own K/V): the
+    # compute time of a step; the ring step minus it is communication left
+    # exposed (not hidden under the block kernels).
+    class LocalRing(ra.RingAttention):
+        def _exchange(self, send, recv):
+            recv.copy_(send)
+            return []
+
+    local_ring = LocalRing()
+
+    def compute_step():
+        o, lse = local_ring.forward(q, k, v)
+        local_ring.backward(q, k, v, o, lse, do)
+
+    for _ in range(2):
+        compute_step()
+    ms_compute = timed(compute_step, args.steps)
+    kv_hop_bytes = 2 * B * H * Tl * D * 2       # bf16 K and V of this rank's two chunks
+    dkv_hop_bytes = 2 * B * H * Tl * D * 4      # fp32 dK / dV partial sums
     # kernel launches per step: forward = one block kernel per block (the merge is in its epilogue),
     # backward = delta pass + dK/dV + dQ per block; plus per-step zeroing / accumulation and the final
     # conversions
@@ -344,6 +365,12 @@ def run_ring(args, w, rank, world, local):
                     "h2d_bytes_per_step": 4 * nbytes, "d2h_bytes_per_step": 4 * nbytes,
                     "ms_per_step": round(ms_e2e / args.steps, 3), "path": "RingAttention (C ABI block calls)"},
             "gpu_launches": launches * args.steps,
+            "ring": {"compute_only_ms_per_step": round(ms_compute / args.steps, 3),
+                     "exposed_comm_ms_per_step": round((ms - ms_compute) / args.steps, 3),
+                     "hops_per_step": {"kv": world - 1, "dkv": world},
+                     "kv_bytes_per_hop": kv_hop_bytes, "dkv_bytes_per_hop": dkv_hop_bytes,
+                     "note": "compute_only = the same step with each NCCL exchange replaced by a local copy; "
+                             "max over ranks"},
             "roofline": {"kernel": "ring step (all block kernels of one rank)", "bound": "tensor",
                          "achieved": round(per_rank, 1), "peak": peak, "unit": "TFLOP/s",
                          "frac": round(per_rank / peak, 3), "traffic": None},
