@@ -565,6 +565,11 @@ __global__ void __launch_bounds__(BwdConfig<DT, HD>::KV_THREADS, 1)
   const uint32_t tbase = *tmem_holder;
   const uint64_t limit = p.wait_limit_ns;
   (void)n_ktiles;
+  // The dQ kernel, which reads none of this kernel's outputs, is launched
+  // next with programmatic serialization: let its blocks take the SMs this
+  // grid's blocks leave as they finish (every block of this grid has started
+  // by now, after the delta pass it reads had completed).
+  grid_dep_launch_dependents();
 
   if (warp == TMA_WARP) {
     if (lane == 0) {
@@ -1322,6 +1327,10 @@ __global__ void __launch_bounds__(320, 1)
     tc_fence_after();
     tmem_dealloc(tbase, C::Q_TMEM);
   }
+  // Launched with programmatic serialization after the dK/dV kernel: finish
+  // only after it has, so that work queued after this kernel on the stream
+  // (which may overwrite the inputs both read) also runs after the dK/dV kernel.
+  grid_dep_wait();
 }
 
 }  // namespace ctfa

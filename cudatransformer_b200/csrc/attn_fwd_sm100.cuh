@@ -573,7 +573,6 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
       const size_t row_index = (size_t)bh * p.q_rows_alloc + p.q_row0 + q_local;
       DT* orow = reinterpret_cast<DT*>(p.o) + row_index * HD;
       float* orow32 = p.o_f32 != nullptr ? p.o_f32 + row_index * HD : nullptr;
-#pragma unroll
       // this block's logsumexp; with `merge`, the row's running (o, lse) and
       // this block's are combined as o = ca * o_run + cb * O with
       // ca = e^(lse_run - lse_new), cb = e^(lse_blk - lse_new) / l

@@ -497,7 +497,25 @@ int launch_bwd_tc(const Problem& pr, const void* q, const void* k, const void* v
   // persistent: one CTA per SM (or per item when there are fewer items)
   const long long dq_items = (long long)n_qt * BH;
   const unsigned dq_grid = (unsigned)std::min<long long>(dq_items, sm_count());
-  kdq<<<dq_grid, C::THREADS, C::Q_SMEM, stream>>>(q_q, q_k, q_v, q_do, q_km, p, n_qt, (int)dq_items);
+  if (ev == nullptr) {
+    // programmatic serialization: dQ blocks start on the SMs the dK/dV blocks
+    // free as they finish (the dQ kernel reads nothing the dK/dV kernel writes
+    // and waits for it before exiting)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(dq_grid);
+    cfg.blockDim = dim3(C::THREADS);
+    cfg.dynamicSmemBytes = C::Q_SMEM;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kdq, q_q, q_k, q_v, q_do, q_km, p, n_qt, (int)dq_items);
+    if (e != cudaSuccess) return cuda_fail(e, "launch attn_bwd_dq_sm100");
+  } else {  // per-kernel events between the launches: plain stream order
+    kdq<<<dq_grid, C::THREADS, C::Q_SMEM, stream>>>(q_q, q_k, q_v, q_do, q_km, p, n_qt, (int)dq_items);
+  }
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch attn_bwd_dq_sm100");
   record(ev, 3, stream);

@@ -453,6 +453,15 @@ __device__ __forceinline__ void regs_decrease() {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
+// Programmatic dependent launch.  launch_dependents: the kernel launched next
+// on the stream with programmatic serialization may start once every block of
+// this grid has executed it (or exited).  wait: block until the grid this one
+// depends on has completed and its memory is visible.
+__device__ __forceinline__ void grid_dep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
