@@ -181,6 +181,9 @@ __device__ __forceinline__ void attn_bwd_prep_rowgroup(const BwdPrepParams& p, l
 template <typename DT, int HD>
 __global__ void __launch_bounds__(256) attn_bwd_prep(BwdPrepParams p) {
   constexpr int TPR = PrepShape<DT, HD>::TPR;
+  // launched with programmatic serialization after the forward: o and lse
+  // are read only once it has completed
+  grid_dep_wait();
   const long long stride = (long long)gridDim.x * blockDim.x;
   const long long total = p.rows * TPR;
   for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t - (threadIdx.x & 31) < total; t += stride)
@@ -565,6 +568,9 @@ __global__ void __launch_bounds__(BwdConfig<DT, HD>::KV_THREADS, 1)
   const uint32_t tbase = *tmem_holder;
   const uint64_t limit = p.wait_limit_ns;
   (void)n_ktiles;
+  // Launched with programmatic serialization after the delta pass: the set-up
+  // above overlaps its tail, everything below reads its output.
+  grid_dep_wait();
   // The dQ kernel, which reads none of this kernel's outputs, is launched
   // next with programmatic serialization: let its blocks take the SMs this
   // grid's blocks leave as they finish (every block of this grid has started

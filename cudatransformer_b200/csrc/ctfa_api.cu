@@ -408,6 +408,31 @@ int launch_bwd_simt(const Problem& pr, const void* q, const void* k, const void*
   return e == cudaSuccess ? CTFA_OK : cuda_fail(e, "launch attn_bwd_simt");
 }
 
+// Launch `kern` on `stream`; with `pdl`, with programmatic stream
+// serialization, so that its blocks may start while the previous kernel on the
+// stream finishes (each kernel launched this way runs griddepcontrol.wait
+// before it touches what the previous kernel writes).  Without it (per-kernel
+// timing events between the launches) an ordinary launch.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_after_previous(bool pdl, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                  cudaStream_t stream, Args... args) {
+  if (!pdl) {
+    kern<<<grid, block, smem, stream>>>(args...);
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 template <typename DT, int HD>
 int launch_bwd_tc(const Problem& pr, const void* q, const void* k, const void* v, const void* o, const void* dO,
                   const void* dO_mma, const float* lse, void* dq, void* dk, void* dv, void* ws, cudaStream_t stream,
@@ -433,9 +458,12 @@ int launch_bwd_tc(const Problem& pr, const void* q, const void* k, const void* v
   if (!std::is_same<DT, float>::value) record(ev, 0, stream);
   const long long prep_blocks =
       std::max<long long>(1, std::min<long long>((pp.rows * PrepShape<DT, HD>::TPR + 255) / 256, sm_count() * 8));
-  attn_bwd_prep<DT, HD><<<(unsigned)prep_blocks, 256, 0, stream>>>(pp);
+  // programmatic serialization after whatever kernel precedes on the stream
+  // (normally the forward): the prep kernel waits for it before reading o / lse
+  cudaError_t e = launch_after_previous(ev == nullptr, attn_bwd_prep<DT, HD>, dim3((unsigned)prep_blocks), dim3(256), 0,
+                                        stream, pp);
   record(ev, 1, stream);
-  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch attn_bwd_prep");
   // 2. dK/dV (key-stationary) and dQ (query-stationary).  Each kernel has its
   // own box heights; tf32 operands read N-major get a 32-byte-granule map.
@@ -487,8 +515,9 @@ int launch_bwd_tc(const Problem& pr, const void* q, const void* k, const void* v
   // persistent: one CTA per SM (or per item when there are fewer items)
   const long long kv_items = (long long)n_kt * BH;
   const unsigned kv_grid = (unsigned)std::min<long long>(kv_items, sm_count());
-  kdkdv<<<kv_grid, C::KV_THREADS, C::KV_SMEM, stream>>>(kv_q, kv_k, kv_v, kv_do, kv_qm, kv_dom, p, n_kt, (int)kv_items);
-  e = cudaGetLastError();
+  e = launch_after_previous(ev == nullptr, kdkdv, dim3(kv_grid), dim3(C::KV_THREADS), C::KV_SMEM, stream, kv_q, kv_k,
+                            kv_v, kv_do, kv_qm, kv_dom, p, n_kt, (int)kv_items);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch attn_bwd_dkdv_sm100");
   record(ev, 2, stream);
   auto kdq = attn_bwd_dq_sm100<DT, HD>;
@@ -497,25 +526,12 @@ int launch_bwd_tc(const Problem& pr, const void* q, const void* k, const void* v
   // persistent: one CTA per SM (or per item when there are fewer items)
   const long long dq_items = (long long)n_qt * BH;
   const unsigned dq_grid = (unsigned)std::min<long long>(dq_items, sm_count());
-  if (ev == nullptr) {
-    // programmatic serialization: dQ blocks start on the SMs the dK/dV blocks
-    // free as they finish (the dQ kernel reads nothing the dK/dV kernel writes
-    // and waits for it before exiting)
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(dq_grid);
-    cfg.blockDim = dim3(C::THREADS);
-    cfg.dynamicSmemBytes = C::Q_SMEM;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, kdq, q_q, q_k, q_v, q_do, q_km, p, n_qt, (int)dq_items);
-    if (e != cudaSuccess) return cuda_fail(e, "launch attn_bwd_dq_sm100");
-  } else {  // per-kernel events between the launches: plain stream order
-    kdq<<<dq_grid, C::THREADS, C::Q_SMEM, stream>>>(q_q, q_k, q_v, q_do, q_km, p, n_qt, (int)dq_items);
-  }
+  // programmatic serialization: dQ blocks start on the SMs the dK/dV blocks
+  // free as they finish (the dQ kernel reads nothing the dK/dV kernel writes
+  // and waits for it before exiting)
+  e = launch_after_previous(ev == nullptr, kdq, dim3(dq_grid), dim3(C::THREADS), C::Q_SMEM, stream, q_q, q_k, q_v,
+                            q_do, q_km, p, n_qt, (int)dq_items);
+  if (e != cudaSuccess) return cuda_fail(e, "launch attn_bwd_dq_sm100");
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch attn_bwd_dq_sm100");
   record(ev, 3, stream);
