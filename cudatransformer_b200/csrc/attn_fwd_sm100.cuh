@@ -204,6 +204,10 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
   tc_fence_after();
   const uint32_t tbase = *tmem_holder;
   const uint64_t limit = p.wait_limit_ns;
+  // launched with programmatic serialization after the previous kernel on the
+  // stream: nothing below may read the inputs or write the outputs before it
+  // has completed
+  grid_dep_wait();
 
   if (warp >= NQ * 4) {
     // --------------------------- producer warpgroup ---------------------------

@@ -137,6 +137,31 @@ bool tensor_core_shape(const Problem& pr) {
          (pr.D == 64 || pr.D == 128);
 }
 
+// Launch `kern` on `stream`; with `pdl`, with programmatic stream
+// serialization, so that its blocks may start while the previous kernel on the
+// stream finishes (each kernel launched this way runs griddepcontrol.wait
+// before it touches what the previous kernel writes).  Without it (per-kernel
+// timing events between the launches) an ordinary launch.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_after_previous(bool pdl, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                  cudaStream_t stream, Args... args) {
+  if (!pdl) {
+    kern<<<grid, block, smem, stream>>>(args...);
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 // RND (fp32 I/O): q, k, v are the caller's fp32 tensors; the kernel rounds
 // every tile to tf32 in shared memory and writes the rounded copies to
 // rounded[0..2] (same layout) for the backward.
@@ -191,8 +216,12 @@ int launch_fwd_tc(const Problem& pr, const void* q, const void* k, const void* v
   }
   const long long grid = (long long)p.n_groups * p.BH;
   if (grid > 0x7fffffffLL) return fail(CTFA_ERR_UNSUPPORTED, "grid too large");
-  kern<<<(unsigned)grid, C::THREADS, C::SMEM_BYTES, stream>>>(mq, mk, mv, mqr, mkr, mvr, p);
-  e = cudaGetLastError();
+  // programmatic serialization after whatever kernel precedes on the stream:
+  // the forward's set-up overlaps its tail, and the forward waits for it
+  // (griddepcontrol.wait) before reading q / k / v or writing anything
+  e = launch_after_previous(true, kern, dim3((unsigned)grid), dim3(C::THREADS), C::SMEM_BYTES, stream, mq, mk, mv, mqr,
+                            mkr, mvr, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch attn_fwd_sm100");
   return CTFA_OK;
 }
@@ -406,31 +435,6 @@ int launch_bwd_simt(const Problem& pr, const void* q, const void* k, const void*
   record(ev, 3, stream);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? CTFA_OK : cuda_fail(e, "launch attn_bwd_simt");
-}
-
-// Launch `kern` on `stream`; with `pdl`, with programmatic stream
-// serialization, so that its blocks may start while the previous kernel on the
-// stream finishes (each kernel launched this way runs griddepcontrol.wait
-// before it touches what the previous kernel writes).  Without it (per-kernel
-// timing events between the launches) an ordinary launch.
-template <typename... KArgs, typename... Args>
-cudaError_t launch_after_previous(bool pdl, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
-                                  cudaStream_t stream, Args... args) {
-  if (!pdl) {
-    kern<<<grid, block, smem, stream>>>(args...);
-    return cudaGetLastError();
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
 template <typename DT, int HD>
