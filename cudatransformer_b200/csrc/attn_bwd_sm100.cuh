@@ -898,14 +898,28 @@ __global__ void __launch_bounds__(BwdConfig<DT, HD>::KV_THREADS, 1)
         // dS^T = P^T (dP^T - delta) (tf32: times the softmax scale; 16-bit:
         // packed adds / multiplies, the scale goes on dK in the epilogue), 32
         // columns at a time, written in place (tf32) or packed into the
-        // already-read front of the dP buffer.
+        // already-read front of the dP buffer.  16-bit: every dP^T column of
+        // this thread is loaded first, with one wait for all of them (the
+        // packed stores below then overwrite only columns already read).
+        uint32_t dpall[C::ROWS_RING ? HALF : 32];
+        if constexpr (C::ROWS_RING) {
+#pragma unroll
+          for (int ch = 0; ch < HALF / 32; ++ch)
+            tmem_ld32(tbase + lane_off + C::KV_DP + h * HALF + ch * 32, *reinterpret_cast<uint32_t(*)[32]>(dpall + ch * 32));
+          tmem_wait_ld();
+        }
 #pragma unroll
         for (int ch = 0; ch < HALF / 32; ++ch) {
           float dsv[32];
           {
             uint32_t regs[32];
-            tmem_ld32(tbase + lane_off + C::KV_DP + h * HALF + ch * 32, regs);
-            tmem_wait_ld();
+            if constexpr (C::ROWS_RING) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) regs[i] = dpall[ch * 32 + i];
+            } else {
+              tmem_ld32(tbase + lane_off + C::KV_DP + h * HALF + ch * 32, regs);
+              tmem_wait_ld();
+            }
 #pragma unroll
             for (int c4 = 0; c4 < 8; ++c4) {
               const int i = 4 * c4;
