@@ -34,6 +34,11 @@
 //     rounds only dO.  Like the reference's cached output and max/denominator
 //     (FlashAttentionLayer.cu:81-84, :114-127), the cache assumes q, k, v were
 //     not modified in place between the two calls.
+//   * cachedOutput shares the buffer of the tensor computeAttention returns
+//     (the reference keeps a device-to-device copy, FlashAttentionLayer.cu:81-84):
+//     one 4·B·H·T·D-byte copy less per step; a caller that writes into the
+//     returned output before computeBackward must copy it first.  The
+//     reference's callers (AttentionLayer, TransformerBlockLayer) only read it.
 // Errors: every non-zero status from the library throws std::runtime_error
 // (the reference throws from cudaMakeShared and ignores launch errors).
 #include "ModuleLayer.cu"
@@ -88,11 +93,13 @@ struct FlashAttentionLayer {
       cachedRoundedFrom[2] = values.get();
       cachedLSE = lse;
       cachedMaxScores = ctfa_dropin::stream_buffer<DType>(rows);
-      castKernel<float, DType><<<(rows + 255) / 256, 256>>>(lse.get(), cachedMaxScores.get(), rows);
       cachedDenominators = ctfa_dropin::stream_buffer<DType>(rows);
-      fillKernel<DType><<<(rows + 255) / 256, 256>>>(cachedDenominators.get(), rows, (DType)1.0f);
-      cachedOutput = ctfa_dropin::stream_buffer<DType>(output.size());
-      cudaMemcpyAsync(cachedOutput.get(), output.data(), output.size() * sizeof(DType), cudaMemcpyDeviceToDevice, 0);
+      const unsigned blocks = (unsigned)std::min<size_t>((rows + 255) / 256, 1184);
+      ctfa_dropin::legacy_row_caches<DType><<<blocks, 256>>>(lse.get(), cachedMaxScores.get(),
+                                                            cachedDenominators.get(), rows);
+      // the cached output shares the returned tensor's buffer (the reference
+      // copies it, FlashAttentionLayer.cu:81-84)
+      cachedOutput = output.dataPtr();
       cachedBatchSize = batchSize;
       cachedSequenceLength = sequenceLength;
     }

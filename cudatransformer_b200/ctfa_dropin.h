@@ -77,6 +77,17 @@ Tensor<T> stream_tensor(const std::vector<size_t>& shape, bool zero = false) {
   return Tensor<T>(stream_buffer<T>(n, zero), shape);
 }
 
+// The reference layer's per-row caches from the fp32 logsumexp the kernels
+// keep: maxScores = lse, denominators = 1 (so exp(s - max) / denom is still
+// the softmax), in one pass.
+template <typename T>
+__global__ void legacy_row_caches(const float* lse, T* maxScores, T* denominators, size_t rows) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows; i += (size_t)gridDim.x * blockDim.x) {
+    maxScores[i] = (T)lse[i];
+    denominators[i] = (T)1.0f;
+  }
+}
+
 }  // namespace ctfa_dropin
 
 #endif  // CTFA_DROPIN_COMMON_H

@@ -239,8 +239,10 @@ def test_flash_dropin_step_config2(cuda_device):
     drives it (computeAttention with saveStates, computeBackward, clearCache):
     its backward reuses the forward's tf32-rounded q, k, v, so its gradients
     are bitwise those of the Python mirror (which does the same), and its step
-    costs little more than the bare C-ABI calls (the drop-in adds the
-    reference's cached copy of o and stream-ordered allocations)."""
+    costs at most 6 % more than the bare C-ABI calls (measured 3 %: the
+    drop-in adds stream-ordered allocations and one small kernel for the
+    reference's max / denominator caches; its cached output shares the
+    returned tensor's buffer)."""
     import torch
 
     from cudatransformer_b200 import FlashAttentionLayer, _lib
@@ -292,4 +294,4 @@ def test_flash_dropin_step_config2(cuda_device):
     torch.cuda.synchronize()
     bare_ms = s_ev.elapsed_time(e_ev) / 20
     print(f"config-2 step: drop-in {ms.value:.4f} ms, bare C ABI {bare_ms:.4f} ms, ratio {ms.value / bare_ms:.3f}")
-    assert ms.value < 1.10 * bare_ms, (ms.value, bare_ms)
+    assert ms.value < 1.06 * bare_ms, (ms.value, bare_ms)
