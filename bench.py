@@ -949,9 +949,11 @@ def run_config4(args, w):
                         "source": "oracle/nanogpt_oracle.py (fp64, PyTorch)"},
         "cpu_baseline": {"value": round(tokens / cpu_step, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
                          "sample": "one training step of the fp64 restatement on the host cores"},
-        "reference": {"unavailable": "the reference NanoGPT reads/writes past its position-embedding table for "
-                                     "batch > 1 (embedding_kernels.cu:64-76) and its AttentionLayer backward divides "
-                                     "by zero (F3); not run"},
+        "reference": {"unavailable": "the reference NanoGPT's embeddings replace the sequence dimension of a "
+                                     "[batch, seq] input with the embedding width (Embedding.cu:43-46, :194-197), so "
+                                     "no [batch, seq, vocab] output or loss curve exists (NanoGPT.cu:92-93); two runs "
+                                     "of it faulted on a B200; its AttentionLayer backward divides by zero (F3); "
+                                     "not run"},
         "clocks": clocks.summary(),
     }
     print(json.dumps(out), flush=True)
