@@ -53,7 +53,11 @@ struct BwdPrepParams {
   float* ndelta;     // [BH][Tq_pad] -delta; 0 on padding rows
   float* nlse2;      // [BH][Tq_pad] -lse * log2(e); -inf on padding rows (their P is 0)
   float* dO_round;   // fp32 I/O only: round-to-nearest tf32 copy of dO (nullable)
+  int* item_counters;  // [2] work-list counters of the dK/dV and dQ kernels, zeroed here
 };
+
+// slots of the work-list ring of the persistent dK/dV and dQ kernels (ItemRing)
+constexpr int ITEM_SLOTS = 4;
 
 struct BwdParams {
   int BH;
@@ -72,6 +76,9 @@ struct BwdParams {
   void* dk;          // [BH][k_rows_alloc][HD]
   void* dv;
   int accumulate;    // 0: write dq/dk/dv in the I/O type; 1: add into fp32 dq/dk/dv buffers
+  int dkdv_head_chunk;  // heads per chunk of the dK/dV item order (BH: one chunk)
+  int dq_head_chunk;    // heads per chunk of the dQ item order
+  int* item_counters;   // [2] next unclaimed dK/dV item, dQ item (zeroed by the delta pass)
   unsigned long long wait_limit_ns;
 };
 
@@ -184,6 +191,10 @@ __global__ void __launch_bounds__(256) attn_bwd_prep(BwdPrepParams p) {
   // launched with programmatic serialization after the forward: o and lse
   // are read only once it has completed
   grid_dep_wait();
+  if (blockIdx.x == 0 && threadIdx.x == 0) {  // work-list counters of the dK/dV and dQ kernels that follow
+    p.item_counters[0] = 0;
+    p.item_counters[1] = 0;
+  }
   const long long stride = (long long)gridDim.x * blockDim.x;
   const long long total = p.rows * TPR;
   for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t - (threadIdx.x & 31) < total; t += stride)
@@ -282,13 +293,17 @@ struct BwdConfig {
   static constexpr bool ROWS_RING = !TF32;
   static constexpr int LD_SLOTS = 4;
   static constexpr int LD_BYTES = 2 * KV_QT * 4;
-  static constexpr int NUM_BARS = 32;
-  static constexpr int KV_SMEM =
-      1024 + 2 * BIG_TILE + KV_ST * KV_STAGE_BYTES + (ROWS_RING ? LD_SLOTS * LD_BYTES : 0) + NUM_BARS * 8 + 16;
-  static constexpr int Q_SMEM = 1024 + 2 * BIG_TILE + Q_KST * Q_KSTAGE_BYTES + Q_VST * Q_VSTAGE_BYTES + NUM_BARS * 8 + 16;
+  static constexpr int NUM_BARS = 40;
+  // after the barriers: TMEM address, abort flag, work-list ring
+  static constexpr int TAIL_BYTES = 8 + 4 * ITEM_SLOTS;
+  static constexpr int KV_SMEM = 1024 + 2 * BIG_TILE + KV_ST * KV_STAGE_BYTES + (ROWS_RING ? LD_SLOTS * LD_BYTES : 0) +
+                                 NUM_BARS * 8 + TAIL_BYTES;
+  static constexpr int Q_SMEM =
+      1024 + 2 * BIG_TILE + Q_KST * Q_KSTAGE_BYTES + Q_VST * Q_VSTAGE_BYTES + NUM_BARS * 8 + TAIL_BYTES;
   static constexpr int THREADS = 320;  // dQ kernel: 8 compute warps, TMA warp, MMA warp
   static_assert(KV_ST >= 1 && Q_KST >= 1 && Q_VST >= 1, "shared memory budget");
-  static_assert(10 + 2 * KV_PARTS * KV_ST + 2 * LD_SLOTS <= NUM_BARS, "dK/dV kernel barriers");
+  static_assert(10 + 2 * KV_PARTS * KV_ST + 2 * LD_SLOTS + 2 * ITEM_SLOTS <= NUM_BARS, "dK/dV kernel barriers");
+  static_assert(9 + 2 * Q_KST + 2 * Q_VST + 2 * ITEM_SLOTS <= NUM_BARS, "dQ kernel barriers");
   static_assert(KV_SMEM <= 232448, "dK/dV kernel shared memory");
   static_assert(Q_SMEM <= 232448, "dQ kernel shared memory");
   static_assert(KV_DV + HD <= 512 && Q_DQ + HD <= 512, "TMEM budget");
@@ -458,11 +473,42 @@ __device__ __forceinline__ void row_store(const uint32_t (&r)[COLS], void* dst, 
   }
 }
 
-// Work item `w` (round-major over a heavy-first order) handled by CTA `c` in
-// round `r` of a boustrophedon assignment: even rounds left to right, odd
-// rounds right to left.  With items sorted by decreasing cost this balances
-// persistent CTAs as well as dynamic scheduling does for these grids.
-__device__ __forceinline__ int snake_item(int r, int c, int G) { return r * G + ((r & 1) ? (G - 1 - c) : c); }
+// Dynamic work list of the persistent backward kernels.  Items are numbered
+// heavy-first inside chunks of heads (head_chunked_item); the TMA warp's lane
+// 0 claims the next unclaimed number from a global counter as it starts an
+// item and publishes it in a ring of ITEM_SLOTS shared-memory slots, from
+// which the MMA and compute warps read the same sequence.  A block's sequence
+// ends at the first number >= n_items it claims.  Blocks taking items as they
+// free up finish within about one item of each other whatever the cost
+// profile of the list; a fixed round-robin assignment balances only lists
+// sorted by decreasing cost, which the head chunks break.  The delta pass
+// that precedes both kernels zeroes their counters.
+
+struct ItemRing {
+  volatile int* slot;  // [ITEM_SLOTS] item numbers
+  uint64_t* full;      // [ITEM_SLOTS] count 1: the producer published the slot
+  uint64_t* empty;     // [ITEM_SLOTS] count = consumer threads: each read it
+
+  // Producer (one thread): claim an item, publish it as sequence entry j.
+  __device__ __forceinline__ bool publish(int j, int* counter, int& w, volatile int* abort, uint64_t limit,
+                                          int site) {
+    w = atomicAdd(counter, 1);
+    const int s = j % ITEM_SLOTS;
+    if (!mbar_wait(&empty[s], ((j / ITEM_SLOTS) & 1) ^ 1, abort, limit, site)) return false;
+    slot[s] = w;
+    mbar_arrive(&full[s]);  // release: the consumers' wait orders their read after the store
+    return true;
+  }
+  // Consumer (every thread of the MMA and compute warps): sequence entry j,
+  // or -1 when the wait gave up.
+  __device__ __forceinline__ int take(int j, volatile int* abort, uint64_t limit, int site) {
+    const int s = j % ITEM_SLOTS;
+    if (!mbar_wait(&full[s], (j / ITEM_SLOTS) & 1, abort, limit, site)) return -1;
+    const int w = slot[s];
+    mbar_arrive(&empty[s]);  // release: orders the read before the producer's reuse
+    return w;
+  }
+};
 
 // ---------------------------------------------------------------------------
 // dK / dV: persistent CTAs; each walks (128-key tile, batch*head) items, heavy
@@ -516,18 +562,20 @@ __global__ void __launch_bounds__(BwdConfig<DT, HD>::KV_THREADS, 1)
   uint64_t* done_bar = acc_free + 1;
   uint64_t* rows_full = done_bar + 1;     // [LDS]
   uint64_t* rows_empty = rows_full + LDS;  // [LDS]
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(rows_empty + LDS);
+  ItemRing items;
+  items.full = rows_empty + LDS;           // [ITEM_SLOTS]
+  items.empty = items.full + ITEM_SLOTS;   // [ITEM_SLOTS]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + C::NUM_BARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  items.slot = abort_flag + 1;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int G = (int)gridDim.x, cta = (int)blockIdx.x;
   const int n_qt_all = (p.Tq + QT - 1) / QT;
   // item -> key tile, batch*head, first query tile that sees the key tile,
   // number of query tiles (causal: heavy key tiles, i.e. low kt, first)
   auto item = [&](int w, int& kt, int& bh, int& qt_first) -> int {
-    kt = w / p.BH;
-    bh = w % p.BH;
+    head_chunked_item(w, p.BH, n_ktiles, p.dkdv_head_chunk, kt, bh);
     qt_first = 0;
     if (p.causal) {
       const int need = kt * C::KV_KEYS - p.causal_offset;  // smallest query index that sees the tile
@@ -554,6 +602,10 @@ __global__ void __launch_bounds__(BwdConfig<DT, HD>::KV_THREADS, 1)
     for (int l = 0; l < LDS; ++l) {
       mbar_init(&rows_full[l], 1);
       mbar_init(&rows_empty[l], CW);  // one arrival per compute warp
+    }
+    for (int l = 0; l < ITEM_SLOTS; ++l) {
+      mbar_init(&items.full[l], 1);
+      mbar_init(&items.empty[l], 32 + CT);  // the MMA warp's and the compute warps' threads
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -590,10 +642,10 @@ __global__ void __launch_bounds__(BwdConfig<DT, HD>::KV_THREADS, 1)
       for (int q = 0; q < NP; ++q) issued[q] = 0;
       int issued_rows = 0;
       bool ok = true;
-      for (int r = 0; ok; ++r) {
-        const int w = snake_item(r, cta, G);
-        if (r * G >= n_items) break;
-        if (w >= n_items) continue;
+      for (int seq = 0; ok; ++seq) {
+        int w;
+        if (!(ok = items.publish(seq, p.item_counters, w, abort_flag, limit, 60))) break;
+        if (w >= n_items) break;
         int kt, bh, qt_first;
         const int n_it = item(w, kt, bh, qt_first);
         if (n_it == 0) continue;
@@ -685,10 +737,10 @@ __global__ void __launch_bounds__(BwdConfig<DT, HD>::KV_THREADS, 1)
     };
     int g = 0, ni = 0;
     bool ok = true;
-    for (int r = 0; ok; ++r) {
-      const int w = snake_item(r, cta, G);
-      if (r * G >= n_items) break;
-      if (w >= n_items) continue;
+    for (int seq = 0; ok; ++seq) {
+      const int w = items.take(seq, abort_flag, limit, 61);
+      if (!(ok = __all_sync(0xffffffffu, w >= 0))) break;
+      if (w >= n_items) break;
       int kt, bh, qt_first;
       const int n_it = item(w, kt, bh, qt_first);
       if (n_it == 0) continue;
@@ -797,10 +849,11 @@ __global__ void __launch_bounds__(BwdConfig<DT, HD>::KV_THREADS, 1)
     const int col = h * (HD / 2);
     int g = 0, ni = 0;
     bool ok = true;
-    for (int r = 0; ok; ++r) {
-      const int w = snake_item(r, cta, G);
-      if (r * G >= n_items) break;
-      if (w >= n_items) continue;
+    for (int seq = 0; ok; ++seq) {
+      const int w = items.take(seq, abort_flag, limit, 62);
+      ok = w >= 0;
+      if (!ok) break;
+      if (w >= n_items) break;
       int kt, bh, qt_first;
       const int n_it = item(w, kt, bh, qt_first);
       const int key0 = kt * C::KV_KEYS;
@@ -1041,18 +1094,22 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* acc_full = ds_full + 1;
   uint64_t* acc_free = acc_full + 1;
   uint64_t* done_bar = acc_free + 1;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(done_bar + 1);
+  ItemRing items;
+  items.full = done_bar + 1;              // [ITEM_SLOTS]
+  items.empty = items.full + ITEM_SLOTS;  // [ITEM_SLOTS]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + C::NUM_BARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  items.slot = abort_flag + 1;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int G = (int)gridDim.x, cta = (int)blockIdx.x;
   const int n_kv_all = (p.Tk + KT - 1) / KT;
   // item -> query tile, batch*head, number of key tiles it sees
   auto item = [&](int w, int& qt, int& bh) -> int {
     if (p.causal) {  // heavy query tiles first
-      qt = n_qtiles - 1 - w / p.BH;
-      bh = w % p.BH;
+      int rank;
+      head_chunked_item(w, p.BH, n_qtiles, p.dq_head_chunk, rank, bh);
+      qt = n_qtiles - 1 - rank;
       const int last_row = min(qt * C::Q_ROWS + C::Q_ROWS - 1, p.Tq - 1) + p.causal_offset;
       return last_row < 0 ? 0 : min(n_kv_all, last_row / KT + 1);
     }
@@ -1079,6 +1136,10 @@ __global__ void __launch_bounds__(320, 1)
     mbar_init(acc_full, 1);
     mbar_init(acc_free, 256);
     mbar_init(done_bar, 1);
+    for (int l = 0; l < ITEM_SLOTS; ++l) {
+      mbar_init(&items.full[l], 1);
+      mbar_init(&items.empty[l], 32 + 256);  // the MMA warp's and the compute warps' threads
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -1101,10 +1162,10 @@ __global__ void __launch_bounds__(320, 1)
       int g = 0, ni = 0;  // key tiles and non-empty items issued so far
       int issued_q = 0, issued_k = 0, issued_v = 0;
       bool ok = true;
-      for (int r = 0; ok; ++r) {
-        const int w = snake_item(r, cta, G);
-        if (r * G >= n_items) break;
-        if (w >= n_items) continue;
+      for (int seq = 0; ok; ++seq) {
+        int w;
+        if (!(ok = items.publish(seq, p.item_counters + 1, w, abort_flag, limit, 63))) break;
+        if (w >= n_items) break;
         int qt, bh;
         const int n_kv = item(w, qt, bh);
         if (n_kv == 0) continue;
@@ -1177,10 +1238,10 @@ __global__ void __launch_bounds__(320, 1)
     };
     int g = 0, ni = 0;
     bool ok = true;
-    for (int r = 0; ok; ++r) {
-      const int w = snake_item(r, cta, G);
-      if (r * G >= n_items) break;
-      if (w >= n_items) continue;
+    for (int seq = 0; ok; ++seq) {
+      const int w = items.take(seq, abort_flag, limit, 64);
+      if (!(ok = __all_sync(0xffffffffu, w >= 0))) break;
+      if (w >= n_items) break;
       int qt, bh;
       const int n_kv = item(w, qt, bh);
       if (n_kv == 0) continue;
@@ -1261,10 +1322,11 @@ __global__ void __launch_bounds__(320, 1)
     const int col = h * (HD / 2);
     int g = 0, ni = 0;
     bool ok = true;
-    for (int r = 0; ok; ++r) {
-      const int w = snake_item(r, cta, G);
-      if (r * G >= n_items) break;
-      if (w >= n_items) continue;
+    for (int seq = 0; ok; ++seq) {
+      const int w = items.take(seq, abort_flag, limit, 65);
+      ok = w >= 0;
+      if (!ok) break;
+      if (w >= n_items) break;
       int qt, bh;
       const int n_kv = item(w, qt, bh);
       const int q = qt * C::Q_ROWS + rr;

@@ -53,6 +53,7 @@ struct FwdParams {
   int causal;          // 0: every key visible; 1: key j visible iff j <= i + causal_offset
   int causal_offset;
   int n_groups;        // CTA groups of NQ query tiles per head
+  int head_chunk;      // causal: heads per chunk of the heavy-first block order (BH: one chunk)
   float scale_log2;    // softmax scale * log2(e)
   void* o;             // [BH][q_rows_alloc][HD] DT
   float* o_f32;        // when set: fp32 output rows here instead of o (block partials)
@@ -147,8 +148,9 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
   // ---- work assignment: heavy query groups first under the causal mask ----
   int group, bh;
   if (p.causal) {
-    group = p.n_groups - 1 - (int)(blockIdx.x / p.BH);
-    bh = (int)(blockIdx.x % p.BH);
+    int rank;
+    head_chunked_item((int)blockIdx.x, p.BH, p.n_groups, p.head_chunk, rank, bh);
+    group = p.n_groups - 1 - rank;
   } else {
     group = (int)(blockIdx.x % p.n_groups);
     bh = (int)(blockIdx.x / p.n_groups);

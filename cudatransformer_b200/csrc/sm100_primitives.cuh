@@ -462,6 +462,19 @@ __device__ __forceinline__ void grid_dep_launch_dependents() {
 }
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// Work item `w` of an n_heads x n_ranks list whose rank 0 is the heaviest
+// tile of every head, walked `chunk` heads at a time: inside a chunk the order
+// is rank-major (the chunk's heaviest tiles first), so the blocks running at
+// one time share a few heads' operands in L2 instead of streaming one head
+// each.  chunk == n_heads is the plain rank-major order.
+__device__ __forceinline__ void head_chunked_item(int w, int n_heads, int n_ranks, int chunk, int& rank, int& head) {
+  const int per = chunk * n_ranks;
+  const int ch = w / per, within = w - ch * per;
+  const int heads = min(chunk, n_heads - ch * chunk);
+  rank = within / heads;
+  head = ch * chunk + within % heads;
+}
+
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
