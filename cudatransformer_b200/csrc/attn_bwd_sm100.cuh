@@ -474,11 +474,12 @@ __device__ __forceinline__ void row_store(const uint32_t (&r)[COLS], void* dst, 
 }
 
 // Dynamic work list of the persistent backward kernels.  Items are numbered
-// heavy-first inside chunks of heads (head_chunked_item); the TMA warp's lane
-// 0 claims the next unclaimed number from a global counter as it starts an
-// item and publishes it in a ring of ITEM_SLOTS shared-memory slots, from
-// which the MMA and compute warps read the same sequence.  A block's sequence
-// ends at the first number >= n_items it claims.  Blocks taking items as they
+// heavy-first inside chunks of heads (head_chunked_item); block b starts with
+// item b (the grid never exceeds the item count), then the TMA warp's lane 0
+// claims the next unclaimed number (gridDim.x + a global counter) as it starts
+// each further item and publishes it in a ring of ITEM_SLOTS shared-memory
+// slots, from which the MMA and compute warps read the same sequence.  A
+// block's sequence ends at the first number >= n_items it claims.  Blocks taking items as they
 // free up finish within about one item of each other whatever the cost
 // profile of the list; a fixed round-robin assignment balances only lists
 // sorted by decreasing cost, which the head chunks break.  The delta pass
@@ -492,7 +493,7 @@ struct ItemRing {
   // Producer (one thread): claim an item, publish it as sequence entry j.
   __device__ __forceinline__ bool publish(int j, int* counter, int& w, volatile int* abort, uint64_t limit,
                                           int site) {
-    w = atomicAdd(counter, 1);
+    w = j == 0 ? (int)blockIdx.x : (int)gridDim.x + atomicAdd(counter, 1);
     const int s = j % ITEM_SLOTS;
     if (!mbar_wait(&empty[s], ((j / ITEM_SLOTS) & 1) ^ 1, abort, limit, site)) return false;
     slot[s] = w;
