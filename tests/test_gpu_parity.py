@@ -124,6 +124,20 @@ def test_many_heads_multi_wave(cuda_device, kind):
         _full_check(ours, q, k, v, do, kind, causal, [(0, 0), (2, 39)])
 
 
+@pytest.mark.parametrize("kind,shape", [("f32", (5, 15, 2048, 64)), ("bf16", (1, 36, 4096, 128))])
+def test_head_chunked_order_with_a_partial_last_chunk(cuda_device, kind, shape):
+    """Heads whose streamed operands exceed 64 MiB together are walked in
+    chunks of 16 MiB worth of heads (fp32 D=64 T=2048: 16 heads of 1 MiB, 75
+    heads = four chunks and one of 11; bf16 D=128 T=4096: 8 heads of 2 MiB, 36
+    heads = four chunks and one of 4), and the persistent backward kernels
+    claim those items dynamically: every head checked, causal and not."""
+    B, H, T, D = shape
+    q, k, v, do = orc.make_inputs(B, H, T, D, seed=41, do_scale=0.1)
+    for causal in (True, False):
+        ours = run_library(q, k, v, do, kind, causal, cuda_device, keep_torch=True)
+        _full_check(ours, q, k, v, do, kind, causal, [(0, 0), (B - 1, H - 1)])
+
+
 @pytest.mark.parametrize("kind", ["f32", "bf16"])
 def test_deterministic(cuda_device, kind):
     """No atomics anywhere: two runs are bitwise identical."""
