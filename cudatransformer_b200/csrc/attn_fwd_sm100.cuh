@@ -60,6 +60,8 @@ struct FwdParams {
   float* lse;          // [BH][q_rows_alloc] natural-log logsumexp (nullable)
   int merge;           // with o_f32: o_f32 / lse hold a running (o, lse) of earlier key blocks,
                        // which this block is folded into (logsumexp-weighted) instead of overwriting
+  int o_tma;           // O (not o_f32) covers whole heads: each tile is staged in shared memory and
+                       // written by TMA stores through tm_o instead of per-row stores
   unsigned long long wait_limit_ns;
 };
 
@@ -108,7 +110,7 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
     attn_fwd_sm100(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_qr,
                    const __grid_constant__ CUtensorMap tm_kr, const __grid_constant__ CUtensorMap tm_vr,
-                   const FwdParams p) {
+                   const __grid_constant__ CUtensorMap tm_o, const FwdParams p) {
   using C = FwdConfig<DT, HD, NQ, BN, KST, VST>;
   static_assert(!RND || C::EB == 4, "in-kernel rounding is for fp32 I/O");
   constexpr int BM = C::BM;
@@ -571,7 +573,17 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
       mbar_arrive(&p_full[k]);
     }
     // ------------------------------ epilogue ------------------------------
+    // With o_tma the tile's 128 threads stage O in their Q buffer (its last
+    // reader, the tile's last S MMA, completed before o_full) in the 128-byte
+    // swizzled layout of tm_o, and one thread stores it with TMA: coalesced
+    // lines instead of 128 rows written 16 bytes per lane.  Every thread of a
+    // tile with keys takes both named barriers, whatever its waits returned.
     if (n > 0 && ok) ok = mbar_wait(&o_full[k], 0, abort_flag, limit, 9);
+    bool o_stored = false;
+    if (n > 0 && p.o_tma) {
+      if (r == 0 && q_stored) tma_store_wait_read();  // the rounded-Q store has read the buffer
+      named_bar_sync(1 + k, 128);
+    }
     if (n > 0 && ok) {
       tc_fence_after();
       const float inv_l = l > 0.f ? 1.f / l : 0.f;
@@ -598,57 +610,106 @@ __global__ void __launch_bounds__(NQ * 128 + 128, 1)
           lse_new = mx + __logf(wa + wb);
         }
       }
+      if (p.o_tma) {
+        uint8_t* tile = sQ + k * C::Q_TILE_BYTES;
 #pragma unroll
-      for (int c = 0; c < HD / 32; ++c) {
-        uint32_t regs[32];
-        tmem_ld32(o_addr + c * 32, regs);
-        tmem_wait_ld();
-        if (row_ok && orow32 != nullptr) {
-          float4* dst = reinterpret_cast<float4*>(orow32 + c * 32);
-          if (keep) continue;
-          if (p.merge) {
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t regs[32];
+          tmem_ld32(o_addr + c * 32, regs);
+          tmem_wait_ld();
+          // 32 columns: one 128-byte block (fp32) or half of one (16-bit),
+          // 16-byte chunk j of row r at chunk position j ^ (r & 7)
+          uint4 w[C::EB == 4 ? 8 : 4];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const float4 a = dst[i];
-              dst[i] = make_float4(fmaf(a.x, ca, __uint_as_float(regs[4 * i]) * cb),
-                                   fmaf(a.y, ca, __uint_as_float(regs[4 * i + 1]) * cb),
-                                   fmaf(a.z, ca, __uint_as_float(regs[4 * i + 2]) * cb),
-                                   fmaf(a.w, ca, __uint_as_float(regs[4 * i + 3]) * cb));
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              dst[i] = make_float4(__uint_as_float(regs[4 * i]) * inv_l, __uint_as_float(regs[4 * i + 1]) * inv_l,
-                                   __uint_as_float(regs[4 * i + 2]) * inv_l,
-                                   __uint_as_float(regs[4 * i + 3]) * inv_l);
-          }
-        } else if (row_ok) {
-          if constexpr (C::EB == 4) {
-            float4* dst = reinterpret_cast<float4*>(orow + c * 32);
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              dst[i] = make_float4(__uint_as_float(regs[4 * i]) * inv_l, __uint_as_float(regs[4 * i + 1]) * inv_l,
-                                   __uint_as_float(regs[4 * i + 2]) * inv_l,
-                                   __uint_as_float(regs[4 * i + 3]) * inv_l);
-          } else {
-            uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              uint32_t w[4];
+          for (int i = 0; i < (C::EB == 4 ? 8 : 4); ++i) {
+            if constexpr (C::EB == 4) {
+              w[i] = make_uint4(__float_as_uint(__uint_as_float(regs[4 * i]) * inv_l),
+                                __float_as_uint(__uint_as_float(regs[4 * i + 1]) * inv_l),
+                                __float_as_uint(__uint_as_float(regs[4 * i + 2]) * inv_l),
+                                __float_as_uint(__uint_as_float(regs[4 * i + 3]) * inv_l));
+            } else {
+              uint32_t h4[4];
 #pragma unroll
               for (int h = 0; h < 4; ++h) {
                 const float a = __uint_as_float(regs[8 * i + 2 * h]) * inv_l;
                 const float b = __uint_as_float(regs[8 * i + 2 * h + 1]) * inv_l;
-                w[h] = (kFmt == 1) ? pack_bf16x2(a, b) : pack_f16x2(a, b);
+                h4[h] = (kFmt == 1) ? pack_bf16x2(a, b) : pack_f16x2(a, b);
               }
-              dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
+              w[i] = make_uint4(h4[0], h4[1], h4[2], h4[3]);
+            }
+          }
+          const int blk = C::EB == 4 ? c : c / 2;
+          const int chunk0 = C::EB == 4 ? 0 : (c % 2) * 4;
+          uint8_t* row = tile + blk * BM * 128 + r * 128;
+#pragma unroll
+          for (int i = 0; i < (C::EB == 4 ? 8 : 4); ++i)
+            *reinterpret_cast<uint4*>(row + (((chunk0 + i) ^ (r & 7)) * 16)) = w[i];
+        }
+      } else {
+  #pragma unroll
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t regs[32];
+          tmem_ld32(o_addr + c * 32, regs);
+          tmem_wait_ld();
+          if (row_ok && orow32 != nullptr) {
+            float4* dst = reinterpret_cast<float4*>(orow32 + c * 32);
+            if (keep) continue;
+            if (p.merge) {
+  #pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float4 a = dst[i];
+                dst[i] = make_float4(fmaf(a.x, ca, __uint_as_float(regs[4 * i]) * cb),
+                                     fmaf(a.y, ca, __uint_as_float(regs[4 * i + 1]) * cb),
+                                     fmaf(a.z, ca, __uint_as_float(regs[4 * i + 2]) * cb),
+                                     fmaf(a.w, ca, __uint_as_float(regs[4 * i + 3]) * cb));
+              }
+            } else {
+  #pragma unroll
+              for (int i = 0; i < 8; ++i)
+                dst[i] = make_float4(__uint_as_float(regs[4 * i]) * inv_l, __uint_as_float(regs[4 * i + 1]) * inv_l,
+                                     __uint_as_float(regs[4 * i + 2]) * inv_l,
+                                     __uint_as_float(regs[4 * i + 3]) * inv_l);
+            }
+          } else if (row_ok) {
+            if constexpr (C::EB == 4) {
+              float4* dst = reinterpret_cast<float4*>(orow + c * 32);
+  #pragma unroll
+              for (int i = 0; i < 8; ++i)
+                dst[i] = make_float4(__uint_as_float(regs[4 * i]) * inv_l, __uint_as_float(regs[4 * i + 1]) * inv_l,
+                                     __uint_as_float(regs[4 * i + 2]) * inv_l,
+                                     __uint_as_float(regs[4 * i + 3]) * inv_l);
+            } else {
+              uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+  #pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                uint32_t w[4];
+  #pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                  const float a = __uint_as_float(regs[8 * i + 2 * h]) * inv_l;
+                  const float b = __uint_as_float(regs[8 * i + 2 * h + 1]) * inv_l;
+                  w[h] = (kFmt == 1) ? pack_bf16x2(a, b) : pack_f16x2(a, b);
+                }
+                dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
+              }
             }
           }
         }
       }
       if (row_ok && p.lse != nullptr && !keep) p.lse[row_index] = lse_new;
     }
-    if (q_stored) tma_store_wait_all();
+    if (n > 0 && p.o_tma) {
+      fence_proxy_async_smem();
+      named_bar_sync(1 + k, 128);
+      if (r == 0 && ok) {
+        const int row = p.q_row0 + qt * BM;
+#pragma unroll
+        for (int b = 0; b < C::KBLK; ++b)
+          tma_store_3d(&tm_o, sQ + k * C::Q_TILE_BYTES + b * BM * 128, b * C::E128, row, bh);
+        tma_store_commit();
+        o_stored = true;
+      }
+    }
+    if (q_stored || o_stored) tma_store_wait_all();
   }
 
   tc_fence_before();

@@ -216,6 +216,11 @@ int launch_fwd_tc(const Problem& pr, const void* q, const void* k, const void* v
   p.o = o;
   p.o_f32 = pr.o_f32;
   p.merge = pr.merge;
+  // whole-head O in the I/O type: staged tiles stored by TMA (rows past T are
+  // clipped by the map, which ends at the last row)
+  CUtensorMap mo = mq;
+  p.o_tma = (o != nullptr && pr.o_f32 == nullptr && pr.q_row0 == 0 && pr.Tq == pr.q_rows) ? 1 : 0;
+  if (p.o_tma && (s = make_map(&mo, o, pr.dtype, HD, pr.q_rows, pr.B * pr.H, 128)) != CTFA_OK) return s;
   p.lse = lse;
   p.wait_limit_ns = g_wait_limit_ns;
   auto kern = attn_fwd_sm100<DT, HD, NQ, BN, KST, VST, RND>;
@@ -238,7 +243,7 @@ int launch_fwd_tc(const Problem& pr, const void* q, const void* k, const void* v
   // the forward's set-up overlaps its tail, and the forward waits for it
   // (griddepcontrol.wait) before reading q / k / v or writing anything
   e = launch_after_previous(true, kern, dim3((unsigned)grid), dim3(C::THREADS), C::SMEM_BYTES, stream, mq, mk, mv, mqr,
-                            mkr, mvr, p);
+                            mkr, mvr, mo, p);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch attn_fwd_sm100");
   return CTFA_OK;
