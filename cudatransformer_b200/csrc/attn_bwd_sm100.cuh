@@ -515,9 +515,10 @@ struct ItemRing {
 };
 
 // ---------------------------------------------------------------------------
-// dK / dV: persistent CTAs; each walks (128-key tile, batch*head) items, heavy
-// first.  K/V of the next item load once the current item's last S^T / dP^T
-// GEMMs ran; the next item's GEMMs overlap the current epilogue.
+// dK / dV: persistent CTAs; each takes (128-key tile, batch*head) items from
+// the work list (ItemRing: heavy first inside chunks of heads).  K/V of the
+// next item load once the current item's last S^T / dP^T GEMMs ran; the next
+// item's GEMMs overlap the current epilogue.
 // ---------------------------------------------------------------------------
 template <typename DT, int HD>
 __global__ void __launch_bounds__(BwdConfig<DT, HD>::KV_THREADS, 1)
@@ -623,7 +624,6 @@ __global__ void __launch_bounds__(BwdConfig<DT, HD>::KV_THREADS, 1)
   tc_fence_after();
   const uint32_t tbase = *tmem_holder;
   const uint64_t limit = p.wait_limit_ns;
-  (void)n_ktiles;
   // Launched with programmatic serialization after the delta pass: the set-up
   // above overlaps its tail, everything below reads its output.
   grid_dep_wait();
@@ -1056,8 +1056,9 @@ __global__ void __launch_bounds__(BwdConfig<DT, HD>::KV_THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------
-// dQ: persistent CTAs; each walks (128-query tile, batch*head) items, heavy
-// first.  Q/dO of the next item load while the current item's last tiles run;
+// dQ: persistent CTAs; each takes (128-query tile, batch*head) items from the
+// work list (ItemRing: heavy first inside chunks of heads).  Q/dO of the next
+// item load while the current item's last tiles run;
 // the dQ accumulator is read into registers and released before it is written
 // out, so the next item's GEMMs start under the current item's epilogue.
 // ---------------------------------------------------------------------------
