@@ -90,7 +90,10 @@ size_t ctfa_backward_workspace_bytes(int B, int H, int T, int D, int dtype);
  * exact gradients (the reference kernel mixes the query index into the key
  * rows it updates, flash_attention.cu:310-321).  dq/dk/dv are fully written
  * (no zero-filled inputs required).  workspace: device memory of at least
- * ctfa_backward_workspace_bytes(...) bytes, 256-byte aligned.
+ * ctfa_backward_workspace_bytes(...) bytes, 256-byte aligned; it holds the
+ * per-row delta / logsumexp arrays and the work-list counters of the
+ * backward kernels, so calls that may run at the same time (other streams)
+ * need separate workspaces.
  */
 int ctfa_backward(const void* q, const void* k, const void* v, const void* o, const void* dO, const float* lse,
                   void* dq, void* dk, void* dv, void* workspace, size_t workspace_bytes, int B, int H, int T,
