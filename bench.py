@@ -560,7 +560,8 @@ def measure_attention(args, w, B, rank, world, local, with_e2e):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
         # keep the stream busy while the host prepares the forward's launch
         # (tensor-map encoding), so that ev[0] -> ev[1] spans the kernel only
-        torch.cuda._sleep(200_000)
+        if hasattr(torch.cuda, "_sleep"):
+            torch.cuda._sleep(200_000)
         ev[0].record(stream)
         fwd()
         ev[1].record(stream)
